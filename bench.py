@@ -1,0 +1,422 @@
+"""Benchmark of the B200 attention hot path (one JSON line on rank 0).
+
+Workload (the largest single-GPU configuration of the
+paged-decode metric): one Qwen3-8B attention layer in decode -- 32 query /
+8 kv heads, head_dim 128, bf16, block size 256 -- batch 512 with context
+lengths lognormal(median 2048, sigma 0.5) capped at 32768 (seed 0).  The
+configuration leaves sigma open; 0.5 is used.  With N GPUs the attention is
+tensor-parallel by kv head: rank r owns kv heads [r*8/N, (r+1)*8/N) and
+their query heads (nanovllm/models/qwen3.py:29-35), so the total work is
+fixed (strong scaling) and ranks exchange nothing on the data path.
+
+A step is one decode step of that layer: the KV-cache scatter of the 512
+new tokens followed by paged decode attention over every cached token.  The
+per-rank cache (4.8 GB / N) is far larger than the 126 MB L2, so no flush is
+needed between steps.  Inputs are synthetic (random bf16, seeded).
+
+  value      algorithmic HBM bytes of the step / device time (GB/s, all ranks)
+  e2e        the same bytes over the time of the user-facing call
+             (Attention.forward) with host-side inputs copied in and the
+             output copied back inside the timed region
+  roofline   the paged-attention kernel alone: bytes / CUDA-event duration,
+             against MEASURED_PEAKS.json's HBM copy bandwidth
+  cpu_baseline  the numpy oracle of the same math on the host cores
+
+--impl reference times the reference path's math on the host CPU (the
+oracle port; the reference itself is CUDA-only) on the same configuration.
+"""
+import argparse
+import json
+import math
+import os
+import re
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+HQ_TOTAL, HKV_TOTAL, HEAD_DIM, BLOCK = 32, 8, 128, 256
+BATCH, SIGMA, CAP = 512, 0.5, 32768
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    return ap.parse_args()
+
+
+def workload():
+    from oracle.cases import config5_context_lens
+    ctx = config5_context_lens(BATCH, SIGMA, seed=0, cap=CAP)
+    return ctx
+
+
+def step_bytes(ctx, hq, hkv, width):
+    """Algorithmic HBM bytes of one step (per rank): decode + store."""
+    d, e = HEAD_DIM, 2
+    B = len(ctx)
+    decode = int(ctx.sum()) * 2 * hkv * d * e + B * hq * d * e * 2 + 4 * B * (1 + width)
+    store = B * 2 * 2 * hkv * d * e + 4 * B
+    return decode, store
+
+
+def measured_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def profiled_traffic():
+    """DRAM bytes per paged-attention launch from the committed ncu summary (or None)."""
+    p = os.path.join(ROOT, "profiles", "paged_attention_config5.md")
+    try:
+        m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", open(p).read())
+        return float(m.group(1)) if m else None
+    except OSError:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_baseline(ctx, hq, hkv, seconds, per_step=None):
+    """Time the numpy oracle of one decode (+store) over sequences of the batch."""
+    from oracle import attention as oatt
+    from oracle import kv_store
+    from oracle.cases import randn_bf16
+    try:
+        from threadpoolctl import threadpool_info
+        cores = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
+    except Exception:
+        cores = os.cpu_count() or 1
+    rng = np.random.default_rng(0)
+    sample = list(range(24)) if per_step is None else list(range(per_step))
+    data = []
+    for b in sample:
+        c = int(ctx[b])
+        nblk = (c + BLOCK - 1) // BLOCK
+        kc = randn_bf16(rng, (nblk, BLOCK, hkv, HEAD_DIM), 0.09)
+        vc = randn_bf16(rng, (nblk, BLOCK, hkv, HEAD_DIM), 0.09)
+        q = randn_bf16(rng, (1, 1, hq, HEAD_DIM), 0.09)
+        kn = randn_bf16(rng, (1, hkv, HEAD_DIM), 0.09)
+        bt = np.arange(nblk, dtype=np.int32)[None]
+        slot = np.asarray([(c - 1) // BLOCK * BLOCK + (c - 1) % BLOCK], np.int32)
+        data.append((kc, vc, q, kn, bt, np.asarray([c], np.int32), slot))
+
+    def one(item):
+        kc, vc, q, kn, bt, cl, slot = item
+        kv_store.store_kvcache_ref(kn, kn, kc, vc, slot)
+        oatt.paged_attention_ref(q, kc, vc, bt, cl, HEAD_DIM ** -0.5)
+        d, s = step_bytes(cl, hq, hkv, bt.shape[1])
+        return d + s
+
+    one(data[0])  # warm
+    t0 = time.perf_counter()
+    nbytes, n, tokens = 0, 0, 0
+    while True:
+        for item in data:
+            nbytes += one(item)
+            n += 1
+            tokens += int(item[5][0])
+        if time.perf_counter() - t0 >= seconds:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": round(nbytes / dt / 1e9, 4), "unit": "GB/s", "cores": int(cores), "kind": "port",
+            "sample": f"{n} sequence-decodes ({tokens} cached tokens) cycling over the first {len(data)} sequences "
+                      f"of the batch, {hkv} kv / {hq} q heads, numpy fp32 oracle, {dt:.1f} s"}
+
+
+def run_reference(args, rank, world):
+    """Reference arm: the path's math on the host CPU (rank 0 only)."""
+    if rank != 0:
+        return
+    ctx = workload()
+    hq, hkv = HQ_TOTAL // world, HKV_TOTAL // world
+    # each step: one sequence-decode of the batch (bounded so that the run takes ~minutes)
+    from oracle import attention as oatt
+    from oracle import kv_store
+    from oracle.cases import randn_bf16
+    rng = np.random.default_rng(0)
+    items = []
+    for b in range(min(32, BATCH)):
+        c = int(ctx[b])
+        nblk = (c + BLOCK - 1) // BLOCK
+        items.append((randn_bf16(rng, (nblk, BLOCK, hkv, HEAD_DIM), 0.09),
+                      randn_bf16(rng, (nblk, BLOCK, hkv, HEAD_DIM), 0.09),
+                      randn_bf16(rng, (1, 1, hq, HEAD_DIM), 0.09), randn_bf16(rng, (1, hkv, HEAD_DIM), 0.09),
+                      np.arange(nblk, dtype=np.int32)[None], np.asarray([c], np.int32),
+                      np.asarray([c - 1], np.int32)))
+
+    def step(i):
+        kc, vc, q, kn, bt, cl, slot = items[i % len(items)]
+        kv_store.store_kvcache_ref(kn, kn, kc, vc, slot)
+        oatt.paged_attention_ref(q, kc, vc, bt, cl, HEAD_DIM ** -0.5)
+        d, s = step_bytes(cl, hq, hkv, bt.shape[1])
+        return d + s
+
+    for i in range(args.warmup):
+        step(i)
+    t0 = time.perf_counter()
+    nbytes = sum(step(i) for i in range(args.steps))
+    dt = time.perf_counter() - t0
+    try:
+        from threadpoolctl import threadpool_info
+        cores = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
+    except Exception:
+        cores = os.cpu_count() or 1
+    v = nbytes / dt / 1e9
+    line = {"metric": "paged-decode attn HBM GB/s", "value": round(v, 4), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "impl": "reference",
+            "config": config_dict(world, ctx),
+            "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": int(cores), "kind": "port",
+                             "sample": f"each step one sequence-decode (store + attention) cycling over the first "
+                                       f"{len(items)} sequences of the batch; numpy fp32 oracle"},
+            "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def config_dict(world, ctx):
+    return {"workload": "config5: Qwen3-8B attention layer decode (store_kvcache + paged attention)",
+            "batch": BATCH, "q_heads": HQ_TOTAL, "kv_heads": HKV_TOTAL, "head_dim": HEAD_DIM, "block_size": BLOCK,
+            "context_lens": f"lognormal(ln 2048, {SIGMA}) capped {CAP}, seed 0", "sum_ctx": int(ctx.sum()),
+            "parallelism": f"tp{world} (kv-head sharded)",
+            "l2": "no flush: per-step KV bytes per rank >> 126 MB L2"}
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        world = args.gpus if "WORLD_SIZE" not in os.environ else world
+    assert HKV_TOTAL % world == 0, f"{world} GPUs do not divide {HKV_TOTAL} kv heads"
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    import torch
+    import torch.distributed as dist
+    import __graft_entry__
+    pkg = __graft_entry__.load_package()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    ctx = workload()
+    hq, hkv = HQ_TOTAL // world, HKV_TOTAL // world
+    nblk = (ctx + BLOCK - 1) // BLOCK
+    nb = int(nblk.sum())
+    width = int(nblk.max())
+    rng = np.random.default_rng(1)
+    perm = rng.permutation(nb).astype(np.int32)
+    bt_np = np.full((BATCH, width), -1, np.int32)
+    off = np.concatenate([[0], np.cumsum(nblk)])
+    for b in range(BATCH):
+        bt_np[b, :nblk[b]] = perm[off[b]:off[b + 1]]
+    slots_np = np.asarray([bt_np[b, (c - 1) // BLOCK] * BLOCK + (c - 1) % BLOCK for b, c in enumerate(ctx)], np.int32)
+
+    g = torch.Generator(device=dev).manual_seed(100 + rank)
+    kc = (torch.randn(nb, BLOCK, hkv, HEAD_DIM, generator=g, device=dev) * 0.09).to(torch.bfloat16)
+    vc = (torch.randn(nb, BLOCK, hkv, HEAD_DIM, generator=g, device=dev) * 0.09).to(torch.bfloat16)
+    q = (torch.randn(BATCH, hq, HEAD_DIM, generator=g, device=dev) * 0.09).to(torch.bfloat16)
+    kn = (torch.randn(BATCH, hkv, HEAD_DIM, generator=g, device=dev) * 0.09).to(torch.bfloat16)
+    vn = (torch.randn(BATCH, hkv, HEAD_DIM, generator=g, device=dev) * 0.09).to(torch.bfloat16)
+    bt = torch.from_numpy(bt_np).to(dev)
+    cl = torch.from_numpy(ctx).to(dev)
+    slots = torch.from_numpy(slots_np).to(dev)
+    out = torch.empty(BATCH, 1, hq, HEAD_DIM, dtype=torch.bfloat16, device=dev)
+    scale = HEAD_DIM ** -0.5
+    ws = pkg.paged_workspace(dev, 1, hq // hkv, BATCH * hkv)
+
+    def step():
+        pkg.store_kvcache(kn, vn, kc, vc, slots)
+        pkg.paged_attention(q.unsqueeze(1), kc, vc, cl, bt, scale, out=out, workspace=ws)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize(dev)
+    # -- timed region: K steps on the device, max over ranks
+    with ClockSampler(local) as clk:
+        barrier()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+    ms = e0.elapsed_time(e1)
+    # -- the dominant kernel alone (paged attention), CUDA events on its stream
+    nk = max(20, min(args.steps, 200))
+    k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    k0.record(stream)
+    for _ in range(nk):
+        pkg.paged_attention(q.unsqueeze(1), kc, vc, cl, bt, scale, out=out, workspace=ws)
+    k1.record(stream)
+    torch.cuda.synchronize(dev)
+    kern_ms = k0.elapsed_time(k1) / nk
+    assert pkg.workspace_error(ws) == 0, "device wait timed out"
+
+    # -- e2e: the user-facing Attention.forward with host inputs and output read-back
+    from learn_nano_vllm_b200 import context as pctx
+    attn = pkg.Attention(hq, HEAD_DIM, scale, hkv)
+    attn.k_cache, attn.v_cache = kc, vc
+    h_q = q.cpu().pin_memory()
+    h_k, h_v = kn.cpu().pin_memory(), vn.cpu().pin_memory()
+    h_bt, h_cl, h_sl = bt.cpu().pin_memory(), cl.cpu().pin_memory(), slots.cpu().pin_memory()
+    h_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    d_q, d_k, d_v = torch.empty_like(q), torch.empty_like(kn), torch.empty_like(vn)
+    d_bt, d_cl, d_sl = torch.empty_like(bt), torch.empty_like(cl), torch.empty_like(slots)
+    h2d = sum(t.numel() * t.element_size() for t in (h_q, h_k, h_v, h_bt, h_cl, h_sl))
+    d2h = h_out.numel() * h_out.element_size()
+
+    def e2e_step():
+        for d, h in ((d_q, h_q), (d_k, h_k), (d_v, h_v), (d_bt, h_bt), (d_cl, h_cl), (d_sl, h_sl)):
+            d.copy_(h, non_blocking=True)
+        pctx.set_context(False, slot_mapping=d_sl, context_lens=d_cl, block_tables=d_bt)
+        o = attn(d_q, d_k, d_v)
+        h_out.copy_(o, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    ne = max(10, min(args.steps, 200))
+    torch.cuda.synchronize(dev)
+    barrier()
+    x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    x0.record(stream)
+    for _ in range(ne):
+        e2e_step()
+    x1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    e2e_ms = x0.elapsed_time(x1) / ne
+    pctx.reset_context()
+
+    dec_b, store_b = step_bytes(ctx, hq, hkv, width)
+    t = torch.tensor([ms, kern_ms, e2e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, kern_ms, e2e_ms = t.tolist()
+    total_bytes = (dec_b + store_b) * world
+    value = total_bytes * args.steps / (ms / 1e3) / 1e9
+    peak, peak_kind = measured_peak()
+    achieved = dec_b / (kern_ms / 1e3) / 1e9
+
+    allreduce = None
+    if world > 1:  # the row-parallel all-reduce that follows o_proj (linear.py:155): [512, 4096] bf16
+        y = torch.randn(BATCH, HQ_TOTAL * HEAD_DIM, device=dev).to(torch.bfloat16)
+        for _ in range(5):
+            dist.all_reduce(y)
+        torch.cuda.synchronize(dev)
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record(stream)
+        for _ in range(50):
+            dist.all_reduce(y)
+        a1.record(stream)
+        torch.cuda.synchronize(dev)
+        at = torch.tensor([a0.elapsed_time(a1) / 50], dtype=torch.float64, device=dev)
+        dist.all_reduce(at, op=dist.ReduceOp.MAX)
+        allreduce = {"bytes": y.numel() * 2, "us": round(at.item() * 1e3, 2), "note": "NCCL, outside the timed region"}
+
+    if rank == 0:
+        line = {"metric": "paged-decode attn HBM GB/s", "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5),
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (seeded random bf16 KV cache, q, new k/v)",
+                "config": config_dict(world, ctx),
+                "e2e": {"value": round((dec_b + store_b) * world / (e2e_ms / 1e3) / 1e9, 2), "unit": "GB/s",
+                        "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+                        "ms_per_step": round(e2e_ms, 5), "api": "Attention.forward (decode), pinned host buffers"},
+                "roofline": {"bound": "hbm", "kernel": "paged_attention_kernel", "achieved": round(achieved, 1),
+                             "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                             "traffic": profiled_traffic(), "bytes_per_launch": int(dec_b),
+                             "us_per_launch": round(kern_ms * 1e3, 2)},
+                "gpu_launches": 2 * args.steps,
+                "clocks": clk.summary()}
+        if allreduce:
+            line["allreduce"] = allreduce
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(ctx, hq, hkv, args.cpu_seconds)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

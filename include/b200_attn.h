@@ -1,0 +1,172 @@
+/*
+ * b200_attn.h — C ABI of the B200 (sm_100a) attention hot path of nano-vLLM.
+ *
+ * Every entry point takes plain device pointers, element strides and sizes,
+ * enqueues its kernels on the caller's CUDA stream (a `cudaStream_t` passed
+ * as `void*`), never synchronises the host, never allocates device memory
+ * and never reads device data on the host.  That makes each call capturable
+ * in a CUDA graph, which is how nano-vLLM runs decode
+ * (nanovllm/engine/model_runner.py:222-257).
+ *
+ * Return value: B200_OK or one of the error codes below.  The text of the
+ * last error of the calling host thread is available from b200_last_error().
+ * Argument checks mirror the `assert`s of the reference launcher
+ * (nanovllm/layers/attention.py:36-39); a failed check launches nothing.
+ *
+ * Tensor conventions (all row-major, element strides):
+ *   token rows  : [N, H, D] with the head dimension contiguous and the head
+ *                 stride equal to D; the token stride is passed explicitly so
+ *                 that the strided `v` view produced by the fused QKV
+ *                 projection (nanovllm/models/qwen3.py:79-82) is accepted.
+ *   KV cache    : one layer of nano-vLLM's cache, [num_blocks, block_size,
+ *                 Hkv, D] contiguous (model_runner.py:113-120).
+ *   block table : int32 [batch, block_table_stride], entries past a
+ *                 sequence's last block are never read (model_runner.py:125).
+ */
+#ifndef B200_ATTN_H
+#define B200_ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define B200_API __attribute__((visibility("default")))
+#else
+#define B200_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum b200_status {
+    B200_OK = 0,
+    B200_ERR_ARG = 1,         /* argument check failed (reference: AssertionError) */
+    B200_ERR_UNSUPPORTED = 2, /* shape or dtype outside what the kernels implement */
+    B200_ERR_WORKSPACE = 3,   /* workspace missing, misaligned or too small */
+    B200_ERR_CUDA = 4         /* the CUDA runtime or driver reported an error */
+};
+
+enum b200_dtype { B200_F16 = 0, B200_BF16 = 1, B200_F32 = 2 };
+
+/* Message of the last failed call on this host thread ("" if none). */
+B200_API const char* b200_last_error(void);
+
+/* Bumped whenever a signature below changes. */
+B200_API int32_t b200_abi_version(void);
+
+/*
+ * KV-cache scatter.  Replaces nanovllm/layers/attention.py:33-40
+ * (`store_kvcache`, Triton kernel at :10-30):
+ *     k_cache.view(-1, Hkv*D)[slot_mapping[t]] = key[t]   (same for value)
+ * for every token t with slot_mapping[t] != -1.  Rows whose slot lies outside
+ * [0, num_slots) are skipped as well (the reference would write out of
+ * bounds).  Non-negative slots must be unique within one call, as in the
+ * reference.  elem_bytes is 2 (bf16/fp16) or 4 (fp32); the copy is bitwise.
+ */
+B200_API int32_t b200_store_kvcache(const void* key, int64_t key_stride,
+                           const void* value, int64_t value_stride,
+                           void* k_cache, void* v_cache,
+                           const int32_t* slot_mapping, int32_t num_tokens,
+                           int32_t num_kv_heads, int32_t head_dim,
+                           int64_t num_slots, int32_t elem_bytes, void* stream);
+
+/*
+ * Paged multi-query attention over the KV cache: decode (query_len == 1)
+ * and speculative verify (query_len == k+1).  Replaces the decode call of
+ * nanovllm/layers/attention.py:71-74:
+ *     flash_attn_with_kvcache(q.unsqueeze(1), k_cache, v_cache,
+ *                             cache_seqlens=context_lens,
+ *                             block_table=block_tables,
+ *                             softmax_scale=scale, causal=True)
+ * q   : [batch, query_len, Hq, D], token stride q_stride_token
+ * out : [batch, query_len, Hq, D] contiguous, same dtype as q
+ * context_lens[b] counts every cached token of sequence b including its
+ * query_len new ones; query j of sequence b sees cache positions
+ * p <= context_lens[b] - query_len + j (causal, bottom-right aligned).
+ * Rows with context_lens[b] <= 0 (CUDA-graph padding) get a zero output.
+ * kv head of query head h is h / (Hq / Hkv) (GQA).
+ * workspace: b200_paged_attention_workspace_size() bytes, 256-byte aligned,
+ * zero-filled once before the first call; every call leaves its control
+ * region zeroed again.  Calls sharing a workspace must not overlap on the GPU.
+ * Constraints: D == 128, dtype bf16 or fp16, block_size % 64 == 0,
+ * batch <= 4096, query_len * (Hq / Hkv) <= 16.
+ */
+B200_API size_t b200_paged_attention_workspace_size(int32_t max_items, int32_t query_len,
+                                           int32_t group_size, int32_t head_dim);
+
+B200_API int32_t b200_paged_attention(void* out, const void* q, int64_t q_stride_token,
+                             const void* k_cache, const void* v_cache,
+                             int32_t num_blocks, int32_t block_size,
+                             const int32_t* block_tables, int32_t block_table_stride,
+                             const int32_t* context_lens, int32_t batch,
+                             int32_t query_len, int32_t num_heads,
+                             int32_t num_kv_heads, int32_t head_dim,
+                             float softmax_scale, int32_t dtype,
+                             void* workspace, size_t workspace_bytes,
+                             void* stream);
+
+/*
+ * Copies the workspace's device-side error word to *flag (synchronously on
+ * `stream`).  Non-zero means a bounded wait inside a kernel gave up; the
+ * results of that call are undefined.  For tests and diagnostics only.
+ */
+B200_API int32_t b200_workspace_error(const void* workspace, void* stream, int32_t* flag);
+
+/*
+ * Causal varlen prefill attention, optionally over the paged cache (prefix
+ * caching / chunked prefill).  Replaces nanovllm/layers/attention.py:64-70:
+ *     flash_attn_varlen_func(q, k, v, cu_seqlens_q=..., cu_seqlens_k=...,
+ *                            max_seqlen_q=..., max_seqlen_k=...,
+ *                            softmax_scale=scale, causal=True,
+ *                            block_table=block_tables)
+ * q/out : [total_q, Hq, D] (out contiguous)
+ * Without a block table k/v are packed token rows [total_k, Hkv, D] and the
+ * keys of sequence s are rows cu_seqlens_k[s] .. cu_seqlens_k[s+1]-1.
+ * With a block table k/v are the layer's caches [num_blocks, block_size,
+ * Hkv, D] and key position p of sequence s lives in block
+ * block_tables[s][p / block_size].  Query i of a sequence with Lq queries and
+ * Lk keys sees key positions p <= i + Lk - Lq (bottom-right causal mask).
+ * Constraints: D == 128, dtype bf16 or fp16, block_size % 128 == 0.
+ */
+B200_API int32_t b200_varlen_prefill(void* out, const void* q, int64_t q_stride_token,
+                            const void* k, int64_t k_stride_token,
+                            const void* v, int64_t v_stride_token,
+                            const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k,
+                            int32_t num_seqs, int32_t max_seqlen_q, int32_t max_seqlen_k,
+                            int32_t total_k_rows,
+                            const int32_t* block_tables, int32_t block_table_stride,
+                            int32_t block_size,
+                            int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
+                            float softmax_scale, int32_t dtype, void* stream);
+
+/*
+ * Speculative-decoding acceptance sampling (standard rejection scheme):
+ * for draft position i = 0..k-1 with draft token x_i, accept when
+ *     u_i < min(1, p_i(x_i) / q_i(x_i))
+ * with p = softmax(target_logits / T), q = softmax(draft_logits / T); at the
+ * first rejection sample from normalise(max(p_i - q_i, 0)), and when all k
+ * drafts are accepted sample a bonus token from p_k.  Sampling uses the
+ * uniform uniform_sample[b] through a fixed-order inverse CDF, so that
+ * results are reproducible bit for bit.  The reference engine has no
+ * speculative path; this op has no counterpart there.
+ * target_logits [batch, k+1, V], draft_logits [batch, k, V] fp32;
+ * draft_tokens, uniform_accept [batch, k]; uniform_sample [batch];
+ * temperatures [batch] or NULL (T = 1).
+ * out_tokens [batch, k+1] int32 (accepted drafts, then the sampled token,
+ * then -1), out_num_tokens [batch] = accepted + 1.
+ */
+B200_API size_t b200_spec_accept_workspace_size(int32_t batch, int32_t num_draft, int32_t vocab_size);
+
+B200_API int32_t b200_spec_accept(int32_t* out_tokens, int32_t* out_num_tokens,
+                         const float* target_logits, const float* draft_logits,
+                         const int32_t* draft_tokens, const float* uniform_accept,
+                         const float* uniform_sample, const float* temperatures,
+                         int32_t batch, int32_t num_draft, int32_t vocab_size,
+                         void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200_ATTN_H */

@@ -1,0 +1,24 @@
+"""B200-native (sm_100a) attention hot path for nano-vLLM.
+
+Import name: `learn_nano_vllm_b200` (the directory name carries hyphens; the
+repository's `__graft_entry__.load_package()` registers it under this name).
+
+Public API
+  Attention                 drop-in for nanovllm.layers.attention.Attention
+  store_kvcache             drop-in for nanovllm.layers.attention.store_kvcache
+  flash_attn_with_kvcache   paged decode / verify attention (decode call site)
+  flash_attn_varlen_func    causal varlen prefill, optionally over the paged cache
+  paged_attention           the same decode kernel with explicit arguments
+  spec_accept               speculative acceptance sampling
+  install                   patch nano-vLLM to use this package's Attention
+  context                   mirror of nanovllm.utils.context
+"""
+from . import context
+from ._native import B200Error, lib
+from .attention import Attention
+from .integrate import install
+from .ops import (flash_attn_varlen_func, flash_attn_with_kvcache, paged_attention, paged_workspace, spec_accept,
+                  store_kvcache, workspace_error)
+
+__all__ = ["Attention", "B200Error", "context", "flash_attn_varlen_func", "flash_attn_with_kvcache", "install",
+           "lib", "paged_attention", "paged_workspace", "spec_accept", "store_kvcache", "workspace_error"]

@@ -1,0 +1,599 @@
+// Paged multi-query attention for decode (query_len 1) and speculative verify
+// (query_len k+1).  Replaces the flash_attn_with_kvcache call of
+// nanovllm/layers/attention.py:71-74.
+//
+// Work decomposition.  A work item is (sequence b, kv head h, chunk c): up to
+// kChunkMaxTiles tiles of 64 cached tokens of one kv head.  All Lq*G query
+// rows that read kv head h (G = Hq/Hkv query heads times Lq queries, at most
+// 16) are processed together, so every K/V byte is read from HBM once.  The
+// chunking is planned on the device from context_lens (no host sync, so the
+// call is CUDA-graph capturable): every CTA scans context_lens into shared
+// memory, picks a chunk length that gives ~kWaves items per CTA, and claims
+// items dynamically from an atomic counter in the workspace.  Items of a
+// sequence that was split write normalised partial outputs plus their
+// log-sum-exp to the workspace; the CTA that finishes the last chunk of a
+// (b, h) merges them (threadfence-reduction pattern) and writes the output.
+//
+// CTA layout: one persistent CTA per SM, 5 warps.  Warp 4 is the producer:
+// one lane issues 2-D TMA loads (no multicast) of 64x64-element boxes with
+// 128-byte swizzle into a kStages-deep ring of 32 KiB stages (K lo/hi dims,
+// V lo/hi dims) guarded by full/empty mbarriers, and writes a small header
+// per stage describing the tile.  Warps 0-3 are consumers: each takes 16 of
+// the 64 tokens of a stage, computes S = Q K^T and O += P V with
+// mma.sync.m16n8k16 (rows = query rows, padded to 16), and keeps its own
+// online-softmax state (max, sum, O) in registers with warp-shuffle row
+// reductions; the four partial states are combined through shared memory at
+// the end of an item.
+#include <climits>
+
+#include "common.cuh"
+
+namespace b200 {
+namespace pa {
+
+constexpr int kTile = 64;
+constexpr int kD = 128;
+constexpr int kStages = 5;
+constexpr int kConsumerWarps = 4;
+constexpr int kConsumers = kConsumerWarps * 32;
+constexpr int kThreads = kConsumers + 32;
+constexpr int kHalfBytes = kTile * 128;      // 64 tokens x 64 dims x 2 B
+constexpr int kStageBytes = 4 * kHalfBytes;  // K dims 0-63, K 64-127, V 0-63, V 64-127
+constexpr int kMaxBatch = 4096;
+constexpr int kCounterSlots = 65536;
+constexpr int kCtrlWords = 64;               // [0] next item, [1] finished CTAs, [2] error word
+constexpr size_t kFixedBytes = kCtrlWords * 4 + size_t(kCounterSlots) * 4;
+constexpr int kWaves = 4;
+constexpr int kChunkMaxTiles = 8;
+constexpr int kSplitBarrier = 1;             // named barrier of the consumer warps
+
+struct Header {
+    int32_t item, b, h, tile, flags, ctx, nchunks, chunk;
+};
+enum : int32_t { kFirst = 1, kLast = 2 };
+
+struct Params {
+    const uint16_t* q;
+    int64_t q_stride;
+    uint16_t* out;
+    const int32_t* block_tables;
+    int32_t bt_stride;
+    const int32_t* context_lens;
+    int32_t batch, lq, hq, hkv, group, rows, block_size, num_blocks;
+    float scale_log2;
+    int32_t* ctrl;
+    int32_t* counters;
+    float* part_o;    // [max_items][rows][kD]
+    float* part_lse;  // [max_items][rows]
+    int32_t max_items;
+};
+
+template <int RC>
+struct Smem {
+    uint8_t stages[kStages][kStageBytes];
+    float co[kConsumerWarps][RC][kD];
+    float cm[kConsumerWarps][RC];
+    float cl[kConsumerWarps][RC];
+    Header hdr[kStages];
+    uint64_t full[kStages];
+    uint64_t empty[kStages];
+    int32_t chunk_off[kMaxBatch + 1];
+    int32_t red[kThreads / 32 + 1];
+    int32_t flag;
+    int32_t err;
+};
+
+template <int RC>
+constexpr int smem_bytes() {
+    return int(sizeof(Smem<RC>)) + 1024;
+}
+
+// Block-wide exclusive scan of one int per thread; returns the exclusive
+// prefix and writes the total to *total.  Uses red[] (one slot per warp).
+__device__ __forceinline__ int block_exclusive_scan(int v, int* red, int* total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) red[warp] = x;
+    __syncthreads();
+    int base = 0, tot = 0;
+#pragma unroll
+    for (int w = 0; w < kThreads / 32; ++w) {
+        if (w < warp) base += red[w];
+        tot += red[w];
+    }
+    __syncthreads();
+    *total = tot;
+    return base + x - v;
+}
+
+template <bool BF16, bool ROWS_HI>
+__global__ void __launch_bounds__(kThreads, 1)
+    paged_attention_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtensorMap tmk,
+                           const __grid_constant__ CUtensorMap tmv) {
+    constexpr int RC = ROWS_HI ? 16 : 8;
+    extern __shared__ uint8_t smem_raw[];
+    Smem<RC>& sm = *reinterpret_cast<Smem<RC>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    if (tid == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&sm.full[s], 1);
+            mbar_init(&sm.empty[s], kConsumerWarps);
+        }
+        sm.err = 0;
+        fence_mbar_init();
+    }
+    if (warp == kConsumerWarps && lane == 0) {
+        prefetch_tmap(&tmk);
+        prefetch_tmap(&tmv);
+    }
+
+    // Rows of CUDA-graph padding (context_lens <= 0) get a zero output.
+    const int64_t row_vec = int64_t(p.lq) * p.hq * kD / 8;  // uint4 per batch row
+    for (int b = blockIdx.x; b < p.batch; b += gridDim.x) {
+        if (p.context_lens[b] <= 0) {
+            uint4* o = reinterpret_cast<uint4*>(p.out) + b * row_vec;
+            for (int64_t i = tid; i < row_vec; i += kThreads) o[i] = make_uint4(0, 0, 0, 0);
+        }
+    }
+
+    // ---- plan: tiles per sequence, chunk length, chunk offsets ----------------
+    const int cap = p.bt_stride * p.block_size;  // tokens addressable through the block table
+    const int seg = (p.batch + kThreads - 1) / kThreads;
+    const int lo = min(tid * seg, p.batch), hi = min(lo + seg, p.batch);
+    int my_tiles = 0;
+    for (int b = lo; b < hi; ++b) {
+        const int ctx = min(p.context_lens[b], cap);
+        my_tiles += ctx > 0 ? (ctx + kTile - 1) / kTile : 0;
+    }
+    int total_tiles = 0;
+    block_exclusive_scan(my_tiles, sm.red, &total_tiles);
+    int64_t chunk;
+    {
+        const int64_t want = int64_t(gridDim.x) * kWaves;
+        chunk = (int64_t(total_tiles) * p.hkv + want - 1) / want;
+        chunk = chunk < 1 ? 1 : (chunk > kChunkMaxTiles ? kChunkMaxTiles : chunk);
+        const int64_t budget = p.max_items / p.hkv;
+        if (budget > p.batch) {
+            const int64_t need = (int64_t(total_tiles) + (budget - p.batch) - 1) / (budget - p.batch);
+            if (need > chunk) chunk = need;
+        } else {
+            chunk = int64_t(1) << 30;
+        }
+    }
+    int my_chunks = 0;
+    for (int b = lo; b < hi; ++b) {
+        const int ctx = min(p.context_lens[b], cap);
+        const int64_t nt = ctx > 0 ? (ctx + kTile - 1) / kTile : 0;
+        my_chunks += int((nt + chunk - 1) / chunk);
+    }
+    int total_chunks = 0;
+    int off = block_exclusive_scan(my_chunks, sm.red, &total_chunks);
+    for (int b = lo; b < hi; ++b) {
+        sm.chunk_off[b] = off;
+        const int ctx = min(p.context_lens[b], cap);
+        const int64_t nt = ctx > 0 ? (ctx + kTile - 1) / kTile : 0;
+        off += int((nt + chunk - 1) / chunk);
+    }
+    if (tid == 0) sm.chunk_off[p.batch] = total_chunks;
+    __syncthreads();
+    const int total_items = total_chunks * p.hkv;
+
+    if (warp == kConsumerWarps) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            const uint64_t pol = l2_policy_evict_first();
+            int stage = 0;
+            uint32_t phase = 0;
+            int64_t fills = 0;
+            bool ok = true;
+            int item = atomicAdd(&p.ctrl[0], 1);
+            while (ok && item < total_items) {
+                const int next = atomicAdd(&p.ctrl[0], 1);
+                const int cg = item / p.hkv, h = item - cg * p.hkv;
+                int blo = 0, bhi = p.batch;  // largest b with chunk_off[b] <= cg
+                while (bhi - blo > 1) {
+                    const int mid = (blo + bhi) >> 1;
+                    if (sm.chunk_off[mid] <= cg) blo = mid; else bhi = mid;
+                }
+                const int b = blo;
+                const int c = cg - sm.chunk_off[b];
+                const int nchunks = sm.chunk_off[b + 1] - sm.chunk_off[b];
+                const int ctx = min(p.context_lens[b], cap);
+                const int nt = (ctx + kTile - 1) / kTile;
+                const int t0 = int(c * chunk);
+                const int t1 = int(min(int64_t(nt), t0 + chunk));
+                const int32_t* bt = p.block_tables + int64_t(b) * p.bt_stride;
+                for (int t = t0; t < t1; ++t) {
+                    if (!mbar_wait(&sm.empty[stage], phase ^ 1)) {
+                        atomicOr(&p.ctrl[2], DEV_ERR_WAIT_EMPTY);
+                        ok = false;
+                        break;
+                    }
+                    const int pos = t * kTile;
+                    const int lb = pos / p.block_size;
+                    const int blk = bt[lb];
+                    const int y = (blk >= 0 && blk < p.num_blocks) ? blk * p.block_size + (pos - lb * p.block_size)
+                                                                   : p.num_blocks * p.block_size;
+                    Header& hd = sm.hdr[stage];
+                    hd.item = item;
+                    hd.b = b;
+                    hd.h = h;
+                    hd.tile = t;
+                    hd.flags = (t == t0 ? kFirst : 0) | (t == t1 - 1 ? kLast : 0);
+                    hd.ctx = ctx;
+                    hd.nchunks = nchunks;
+                    hd.chunk = c;
+                    mbar_arrive_expect_tx(&sm.full[stage], kStageBytes);
+                    uint8_t* st = sm.stages[stage];
+                    const int x = h * kD;
+                    tma_load_2d(st, &tmk, x, y, &sm.full[stage], pol);
+                    tma_load_2d(st + kHalfBytes, &tmk, x + 64, y, &sm.full[stage], pol);
+                    tma_load_2d(st + 2 * kHalfBytes, &tmv, x, y, &sm.full[stage], pol);
+                    tma_load_2d(st + 3 * kHalfBytes, &tmv, x + 64, y, &sm.full[stage], pol);
+                    ++fills;
+                    if (++stage == kStages) { stage = 0; phase ^= 1; }
+                }
+                item = next;
+            }
+            if (ok) {
+                if (mbar_wait(&sm.empty[stage], phase ^ 1)) {
+                    sm.hdr[stage].item = -1;  // sentinel: no more tiles
+                    mbar_arrive(&sm.full[stage]);
+                } else {
+                    atomicOr(&p.ctrl[2], DEV_ERR_WAIT_EMPTY);
+                    ok = false;
+                }
+            }
+            if (!ok) {
+                // Error path: wait (bounded) for every TMA fill still in flight
+                // before the CTA's shared memory is released.
+                for (int s = 0; s < kStages; ++s) {
+                    if (fills <= s) break;
+                    const int64_t last = s + ((fills - 1 - s) / kStages) * kStages;
+                    if (!mbar_wait(&sm.full[s], uint32_t((last / kStages) & 1))) atomicOr(&p.ctrl[2], DEV_ERR_WAIT_DRAIN);
+                }
+            }
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------------------ consumers
+        const int g = lane >> 2, t4 = lane & 3;
+        const int mi = lane >> 3, rr = lane & 7;
+        const int tok_k = warp * 16 + (mi >> 1) * 8 + rr;  // ldmatrix row of K (token in tile)
+        const int tok_v = warp * 16 + (mi & 1) * 8 + rr;   // ldmatrix row of V
+        const int kadd = mi & 1, vadd = mi >> 1;
+        const float sl2 = p.scale_log2;
+        int stage = 0;
+        uint32_t phase = 0;
+        float m_run[2], l_run[2];
+        float o[16][4];
+        uint32_t qa[8][4];
+        int lim[2];
+        while (true) {
+            if (!mbar_wait(&sm.full[stage], phase)) {
+                atomicOr(&p.ctrl[2], DEV_ERR_WAIT_FULL);
+                *reinterpret_cast<volatile int32_t*>(&sm.err) = 1;
+                break;
+            }
+            // A sibling consumer warp that gave up will not reach the named
+            // barriers below: leave together instead of waiting for it.
+            if (*reinterpret_cast<volatile int32_t*>(&sm.err)) break;
+            const Header hd = sm.hdr[stage];
+            if (hd.item < 0) break;
+            if (hd.flags & kFirst) {
+#pragma unroll
+                for (int hr = 0; hr < 2; ++hr) {
+                    const int r = g + 8 * hr;
+                    const bool valid = r < p.rows;
+                    const int j = valid ? r / p.group : 0;
+                    const int gq = valid ? r - j * p.group : 0;
+                    lim[hr] = valid ? hd.ctx - p.lq + j : -1;
+                    const uint32_t* qrow = reinterpret_cast<const uint32_t*>(
+                        p.q + (int64_t(hd.b) * p.lq + j) * p.q_stride + int64_t(hd.h * p.group + gq) * kD);
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk) {
+                        qa[kk][hr] = valid ? __ldg(qrow + kk * 8 + t4) : 0u;
+                        qa[kk][2 + hr] = valid ? __ldg(qrow + kk * 8 + 4 + t4) : 0u;
+                    }
+                    m_run[hr] = -INFINITY;
+                    l_run[hr] = 0.f;
+                }
+#pragma unroll
+                for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+            }
+            const int tok_base = hd.tile * kTile + warp * 16;
+            const uint32_t st = smem_u32(sm.stages[stage]);
+            bool zeroed = false;
+            if (tok_base < hd.ctx) {
+                if (tok_base + 16 > hd.ctx) {
+                    // Cache rows past the context may hold anything (NaN bits);
+                    // P is 0 there but 0 * NaN is NaN, so clear those V rows.
+                    const int first = hd.ctx - tok_base;
+                    uint8_t* vb = sm.stages[stage] + 2 * kHalfBytes;
+                    for (int i = lane; i < (16 - first) * 16; i += 32) {
+                        const int row = warp * 16 + first + (i >> 4);
+                        const int half = (i >> 3) & 1, ch = i & 7;
+                        *reinterpret_cast<uint4*>(vb + half * kHalfBytes + row * 128 + ch * 16) = make_uint4(0, 0, 0, 0);
+                    }
+                    zeroed = true;
+                    __syncwarp();
+                }
+                float s[2][4];
+#pragma unroll
+                for (int n = 0; n < 2; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk) {
+                    const int c16 = 2 * kk + kadd;
+                    const uint32_t addr = st + (kk >> 2) * kHalfBytes + tok_k * 128 + (((c16 & 7) ^ rr) << 4);
+                    uint32_t b0, b1, b2, b3;
+                    ldsm_x4(b0, b1, b2, b3, addr);
+                    mma_16816<BF16>(s[0], qa[kk], b0, b1);
+                    mma_16816<BF16>(s[1], qa[kk], b2, b3);
+                }
+                float pr[2][4];
+#pragma unroll
+                for (int hr = 0; hr < (ROWS_HI ? 2 : 1); ++hr) {
+                    float v[4] = {s[0][2 * hr], s[0][2 * hr + 1], s[1][2 * hr], s[1][2 * hr + 1]};
+                    const int tk[4] = {tok_base + 2 * t4, tok_base + 2 * t4 + 1, tok_base + 8 + 2 * t4,
+                                       tok_base + 9 + 2 * t4};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                        if (tk[e] > lim[hr]) v[e] = -INFINITY;
+                    float mx = fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3]));
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+                    const float mnew = fmaxf(m_run[hr], mx);
+                    const float msl = mnew == -INFINITY ? 0.f : mnew * sl2;
+                    const float alpha = fast_exp2(fmaf(m_run[hr], sl2, -msl));
+                    float sum = 0.f;
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        pr[hr][e] = fast_exp2(fmaf(v[e], sl2, -msl));
+                        sum += pr[hr][e];
+                    }
+                    l_run[hr] = fmaf(l_run[hr], alpha, sum);
+                    m_run[hr] = mnew;
+#pragma unroll
+                    for (int n = 0; n < 16; ++n) {
+                        o[n][2 * hr] *= alpha;
+                        o[n][2 * hr + 1] *= alpha;
+                    }
+                }
+                uint32_t pa[4];
+                pa[0] = pack2<BF16>(pr[0][0], pr[0][1]);
+                pa[2] = pack2<BF16>(pr[0][2], pr[0][3]);
+                if constexpr (ROWS_HI) {
+                    pa[1] = pack2<BF16>(pr[1][0], pr[1][1]);
+                    pa[3] = pack2<BF16>(pr[1][2], pr[1][3]);
+                } else {
+                    pa[1] = pa[3] = 0u;
+                }
+#pragma unroll
+                for (int pp = 0; pp < 8; ++pp) {
+                    const int c16 = 2 * pp + vadd;
+                    const uint32_t addr =
+                        st + 2 * kHalfBytes + (pp >> 2) * kHalfBytes + tok_v * 128 + (((c16 & 7) ^ rr) << 4);
+                    uint32_t v0, v1, v2, v3;
+                    ldsm_x4_t(v0, v1, v2, v3, addr);
+                    mma_16816<BF16>(o[2 * pp], pa, v0, v1);
+                    mma_16816<BF16>(o[2 * pp + 1], pa, v2, v3);
+                }
+            }
+            if (zeroed) fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.empty[stage]);
+            if (++stage == kStages) { stage = 0; phase ^= 1; }
+
+            if (hd.flags & kLast) {
+                // ---- combine the four warps' states of this item ----
+#pragma unroll
+                for (int hr = 0; hr < 2; ++hr) {
+                    l_run[hr] += __shfl_xor_sync(0xffffffffu, l_run[hr], 1);
+                    l_run[hr] += __shfl_xor_sync(0xffffffffu, l_run[hr], 2);
+                }
+#pragma unroll
+                for (int hr = 0; hr < (ROWS_HI ? 2 : 1); ++hr) {
+                    const int r = g + 8 * hr;
+                    if (t4 == 0) {
+                        sm.cm[warp][r] = m_run[hr];
+                        sm.cl[warp][r] = l_run[hr];
+                    }
+#pragma unroll
+                    for (int n = 0; n < 16; ++n)
+                        *reinterpret_cast<float2*>(&sm.co[warp][r][8 * n + 2 * t4]) =
+                            make_float2(o[n][2 * hr], o[n][2 * hr + 1]);
+                }
+                named_bar_sync(kSplitBarrier, kConsumers);
+                const bool single = hd.nchunks == 1;
+                const int nel = p.rows * kD;
+                for (int idx = tid; idx < nel; idx += kConsumers) {
+                    const int r = idx >> 7, d = idx & (kD - 1);
+                    float M = -INFINITY;
+#pragma unroll
+                    for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, sm.cm[w][r]);
+                    float den = 0.f, acc = 0.f;
+                    if (M != -INFINITY) {
+#pragma unroll
+                        for (int w = 0; w < kConsumerWarps; ++w) {
+                            const float sc = fast_exp2((sm.cm[w][r] - M) * sl2);
+                            den = fmaf(sm.cl[w][r], sc, den);
+                            acc = fmaf(sm.co[w][r][d], sc, acc);
+                        }
+                    }
+                    const float val = den > 0.f ? acc / den : 0.f;
+                    if (single) {
+                        const int j = r / p.group, gq = r - j * p.group;
+                        p.out[((int64_t(hd.b) * p.lq + j) * p.hq + hd.h * p.group + gq) * kD + d] = to_bits16<BF16>(val);
+                    } else {
+                        p.part_o[(int64_t(hd.item) * p.rows + r) * kD + d] = val;
+                        if (d == 0)
+                            p.part_lse[int64_t(hd.item) * p.rows + r] = den > 0.f ? fmaf(M, sl2, fast_log2(den)) : -INFINITY;
+                    }
+                }
+                if (!single) {
+                    __threadfence();
+                    named_bar_sync(kSplitBarrier, kConsumers);
+                    if (tid == 0) {
+                        const int prev = atomicAdd(&p.counters[hd.b * p.hkv + hd.h], 1);
+                        sm.flag = (prev == hd.nchunks - 1);
+                    }
+                    named_bar_sync(kSplitBarrier, kConsumers);
+                    if (sm.flag) {
+                        __threadfence();
+                        const int64_t item0 = int64_t(sm.chunk_off[hd.b]) * p.hkv + hd.h;
+                        for (int idx = tid; idx < nel; idx += kConsumers) {
+                            const int r = idx >> 7, d = idx & (kD - 1);
+                            float L = -INFINITY;
+                            for (int c = 0; c < hd.nchunks; ++c)
+                                L = fmaxf(L, __ldcg(p.part_lse + (item0 + int64_t(c) * p.hkv) * p.rows + r));
+                            float den = 0.f, acc = 0.f;
+                            if (L != -INFINITY) {
+                                for (int c = 0; c < hd.nchunks; ++c) {
+                                    const int64_t it = item0 + int64_t(c) * p.hkv;
+                                    const float w = fast_exp2(__ldcg(p.part_lse + it * p.rows + r) - L);
+                                    den += w;
+                                    acc = fmaf(w, __ldcg(p.part_o + (it * p.rows + r) * kD + d), acc);
+                                }
+                            }
+                            const int j = r / p.group, gq = r - j * p.group;
+                            p.out[((int64_t(hd.b) * p.lq + j) * p.hq + hd.h * p.group + gq) * kD + d] =
+                                to_bits16<BF16>(den > 0.f ? acc / den : 0.f);
+                        }
+                        if (tid == 0) p.counters[hd.b * p.hkv + hd.h] = 0;
+                    }
+                }
+                named_bar_sync(kSplitBarrier, kConsumers);
+            }
+        }
+    }
+
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        const int done = atomicAdd(&p.ctrl[1], 1);
+        if (done == int(gridDim.x) - 1) {
+            // Every CTA has stopped claiming items: re-arm the scheduler.
+            atomicExch(&p.ctrl[0], 0);
+            atomicExch(&p.ctrl[1], 0);
+        }
+    }
+}
+
+}  // namespace pa
+}  // namespace b200
+
+extern "C" size_t b200_paged_attention_workspace_size(int32_t max_items, int32_t query_len, int32_t group_size,
+                                                      int32_t head_dim) {
+    using namespace b200::pa;
+    if (max_items < 0 || query_len < 1 || group_size < 1 || head_dim < 1) return 0;
+    const size_t rows = size_t(query_len) * group_size;
+    const size_t bytes = kFixedBytes + size_t(max_items) * rows * (size_t(head_dim) + 1) * 4;
+    return (bytes + 255) & ~size_t(255);
+}
+
+extern "C" int32_t b200_paged_attention(void* out, const void* q, int64_t q_stride_token, const void* k_cache,
+                                        const void* v_cache, int32_t num_blocks, int32_t block_size,
+                                        const int32_t* block_tables, int32_t block_table_stride,
+                                        const int32_t* context_lens, int32_t batch, int32_t query_len,
+                                        int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
+                                        float softmax_scale, int32_t dtype, void* workspace, size_t workspace_bytes,
+                                        void* stream) {
+    using namespace b200;
+    using namespace b200::pa;
+    clear_error();
+    B200_REQUIRE(batch >= 0, "paged_attention: batch %d < 0", batch);
+    if (batch == 0) return B200_OK;
+    B200_REQUIRE(out && q && k_cache && v_cache && block_tables && context_lens, "paged_attention: null pointer");
+    B200_REQUIRE(num_heads > 0 && num_kv_heads > 0 && num_heads % num_kv_heads == 0,
+                 "paged_attention: num_heads %d not a multiple of num_kv_heads %d", num_heads, num_kv_heads);
+    B200_REQUIRE(query_len >= 1, "paged_attention: query_len %d < 1", query_len);
+    const int group = num_heads / num_kv_heads;
+    const int rows = query_len * group;
+    if (head_dim != kD) return fail(B200_ERR_UNSUPPORTED, "paged_attention: head_dim %d (only 128)", head_dim);
+    if (rows > 16)
+        return fail(B200_ERR_UNSUPPORTED, "paged_attention: query_len * Hq/Hkv = %d exceeds 16", rows);
+    if (dtype != B200_BF16 && dtype != B200_F16)
+        return fail(B200_ERR_UNSUPPORTED, "paged_attention: dtype %d (bf16 or fp16 only)", dtype);
+    if (batch > kMaxBatch) return fail(B200_ERR_UNSUPPORTED, "paged_attention: batch %d > %d", batch, kMaxBatch);
+    B200_REQUIRE(block_size > 0 && block_size % kTile == 0, "paged_attention: block_size %d not a multiple of %d",
+                 block_size, kTile);
+    B200_REQUIRE(num_blocks > 0 && int64_t(num_blocks) * block_size < (int64_t(1) << 31),
+                 "paged_attention: num_blocks %d out of range", num_blocks);
+    B200_REQUIRE(block_table_stride > 0 && int64_t(block_table_stride) * block_size < (int64_t(1) << 31),
+                 "paged_attention: block_table_stride %d out of range", block_table_stride);
+    B200_REQUIRE(q_stride_token >= int64_t(num_heads) * head_dim && q_stride_token % 2 == 0,
+                 "paged_attention: q token stride %lld", (long long)q_stride_token);
+    B200_REQUIRE((reinterpret_cast<uintptr_t>(q) & 3) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0,
+                 "paged_attention: q must be 4-byte and out 16-byte aligned");
+    if (int64_t(batch) * num_kv_heads > kCounterSlots)
+        return fail(B200_ERR_UNSUPPORTED, "paged_attention: batch * num_kv_heads > %d", kCounterSlots);
+    if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255) || workspace_bytes < kFixedBytes)
+        return fail(B200_ERR_WORKSPACE, "paged_attention: workspace missing, unaligned or smaller than %zu bytes",
+                    kFixedBytes);
+    const int64_t max_items = int64_t(workspace_bytes - kFixedBytes) / (int64_t(rows) * (kD + 1) * 4);
+    if (max_items < int64_t(batch) * num_kv_heads)
+        return fail(B200_ERR_WORKSPACE, "paged_attention: workspace holds %lld items, batch * Hkv = %lld",
+                    (long long)max_items, (long long)batch * num_kv_heads);
+
+    const bool bf16 = dtype == B200_BF16;
+    const uint64_t row_elems = uint64_t(num_kv_heads) * kD;
+    const uint64_t rows_total = uint64_t(num_blocks) * block_size;
+    CUtensorMap tmk, tmv;
+    int32_t rc = make_tmap_2d(&tmk, k_cache, row_elems, rows_total, row_elems * 2, 64, kTile, bf16,
+                              CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    rc = make_tmap_2d(&tmv, v_cache, row_elems, rows_total, row_elems * 2, 64, kTile, bf16,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+
+    Params prm;
+    prm.q = static_cast<const uint16_t*>(q);
+    prm.q_stride = q_stride_token;
+    prm.out = static_cast<uint16_t*>(out);
+    prm.block_tables = block_tables;
+    prm.bt_stride = block_table_stride;
+    prm.context_lens = context_lens;
+    prm.batch = batch;
+    prm.lq = query_len;
+    prm.hq = num_heads;
+    prm.hkv = num_kv_heads;
+    prm.group = group;
+    prm.rows = rows;
+    prm.block_size = block_size;
+    prm.num_blocks = num_blocks;
+    prm.scale_log2 = softmax_scale * 1.4426950408889634f;
+    char* ws = static_cast<char*>(workspace);
+    prm.ctrl = reinterpret_cast<int32_t*>(ws);
+    prm.counters = reinterpret_cast<int32_t*>(ws + kCtrlWords * 4);
+    prm.part_o = reinterpret_cast<float*>(ws + kFixedBytes);
+    prm.part_lse = prm.part_o + max_items * rows * kD;
+    prm.max_items = int32_t(max_items > INT32_MAX / 2 ? INT32_MAX / 2 : max_items);
+
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const dim3 grid(device_sm_count()), block(kThreads);
+    const bool hi = rows > 8;
+    const void* fn;
+    int smem;
+    if (bf16) {
+        fn = hi ? (const void*)paged_attention_kernel<true, true> : (const void*)paged_attention_kernel<true, false>;
+    } else {
+        fn = hi ? (const void*)paged_attention_kernel<false, true> : (const void*)paged_attention_kernel<false, false>;
+    }
+    smem = hi ? smem_bytes<16>() : smem_bytes<8>();
+    ensure_smem_attr(fn, smem);
+    if (bf16) {
+        if (hi) paged_attention_kernel<true, true><<<grid, block, smem, s>>>(prm, tmk, tmv);
+        else paged_attention_kernel<true, false><<<grid, block, smem, s>>>(prm, tmk, tmv);
+    } else {
+        if (hi) paged_attention_kernel<false, true><<<grid, block, smem, s>>>(prm, tmk, tmv);
+        else paged_attention_kernel<false, false><<<grid, block, smem, s>>>(prm, tmk, tmv);
+    }
+    B200_CUDA_TRY(cudaGetLastError());
+    return B200_OK;
+}

@@ -1,0 +1,218 @@
+"""Torch-facing ops of the B200 attention path.
+
+Names and argument meanings follow the calls of the reference hot path
+(nanovllm/layers/attention.py): `store_kvcache` (:33-40), and the two
+flash-attn entry points it uses, `flash_attn_with_kvcache` (:72-74) and
+`flash_attn_varlen_func` (:67-70), restricted to the arguments nano-vLLM
+passes.  Each op checks its tensors, then calls the C ABI of
+libb200attn.so on the current CUDA stream; nothing here synchronises the
+host or computes on the CPU, so the ops can be captured in CUDA graphs.
+"""
+import ctypes
+import threading
+
+import torch
+
+from . import _native
+from ._native import check, lib
+
+_DTYPES = {torch.bfloat16: _native.B200_BF16, torch.float16: _native.B200_F16}
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _require_cuda(*ts):
+    dev = ts[0].device
+    for t in ts:
+        assert t.is_cuda, "B200 attention ops take CUDA tensors"
+        assert t.device == dev, f"tensors on different devices ({t.device} vs {dev})"
+
+
+# ------------------------------------------------------------------ KV store
+def store_kvcache(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                  slot_mapping: torch.Tensor) -> None:
+    """k_cache.view(-1, Hkv*D)[slot] = key[t] (and value) for slot != -1.
+
+    Same contract and asserts as nanovllm/layers/attention.py:33-40; in
+    addition slots outside the cache are skipped instead of written.
+    """
+    N, num_heads, head_dim = key.shape
+    D = num_heads * head_dim
+    assert key.stride(-1) == 1 and value.stride(-1) == 1
+    assert key.stride(1) == head_dim and value.stride(1) == head_dim
+    assert k_cache.stride(1) == D and v_cache.stride(1) == D
+    assert slot_mapping.numel() == N
+    _require_cuda(key, value, k_cache, v_cache, slot_mapping)
+    assert k_cache.is_contiguous() and v_cache.is_contiguous(), "KV caches must be contiguous"
+    assert key.dtype == value.dtype == k_cache.dtype == v_cache.dtype, "key/value/cache dtypes differ"
+    assert slot_mapping.dtype == torch.int32 and slot_mapping.is_contiguous(), "slot_mapping must be contiguous int32"
+    num_slots = k_cache.numel() // D
+    rc = lib().b200_store_kvcache(key.data_ptr(), key.stride(0), value.data_ptr(), value.stride(0),
+                                  k_cache.data_ptr(), v_cache.data_ptr(), slot_mapping.data_ptr(), N,
+                                  num_heads, head_dim, num_slots, key.element_size(), _stream(key))
+    check(rc, "store_kvcache")
+
+
+# --------------------------------------------------------- paged attention
+DEFAULT_MAX_ITEMS = 32768
+_ws_lock = threading.Lock()
+_workspaces: dict[int, torch.Tensor] = {}
+
+
+def paged_workspace(device: torch.device, query_len: int, group: int, min_items: int) -> torch.Tensor:
+    """Per-device split-K workspace for paged attention (zero-filled, grown on demand).
+
+    Growing it allocates, which is not allowed while a CUDA graph is being
+    captured: the first eager call at the largest batch (nano-vLLM's warm-up
+    before capture, model_runner.py:240) sizes it.
+    """
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    items = max(DEFAULT_MAX_ITEMS, min_items)
+    need = lib().b200_paged_attention_workspace_size(items, query_len, group, 128)
+    with _ws_lock:
+        ws = _workspaces.get(idx)
+        if ws is None or ws.numel() < need:
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("paged attention workspace must be allocated before CUDA-graph capture")
+            if ws is not None:
+                torch.cuda.current_stream(device).synchronize()
+            ws = torch.zeros(need, dtype=torch.uint8, device=torch.device("cuda", idx))
+            _workspaces[idx] = ws
+    return ws
+
+
+def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, context_lens: torch.Tensor,
+                    block_tables: torch.Tensor, softmax_scale: float, out: torch.Tensor | None = None,
+                    workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Causal (bottom-right) attention of q [B, Lq, Hq, D] over the paged cache.
+
+    context_lens [B] counts the cached tokens of each row including its Lq
+    queries; rows with context_lens <= 0 return zeros.  Returns
+    [B, Lq, Hq, D] in q's dtype.
+    """
+    B, Lq, Hq, D = q.shape
+    NB, bs, Hkv, Dk = k_cache.shape
+    assert Dk == D and v_cache.shape == k_cache.shape, "cache shape mismatch"
+    assert q.stride(-1) == 1 and q.stride(-2) == D, "q heads must be contiguous"
+    if Lq == 1:
+        q_tok = q.stride(0)
+    else:
+        assert q.stride(0) == Lq * q.stride(1), "q rows of one sequence must be evenly strided"
+        q_tok = q.stride(1)
+    _require_cuda(q, k_cache, v_cache, context_lens, block_tables)
+    assert k_cache.is_contiguous() and v_cache.is_contiguous(), "KV caches must be contiguous"
+    assert q.dtype in _DTYPES and k_cache.dtype == q.dtype == v_cache.dtype, "q/cache dtype must match (bf16/fp16)"
+    assert context_lens.dtype == torch.int32 and context_lens.is_contiguous() and context_lens.numel() == B
+    assert block_tables.dtype == torch.int32 and block_tables.dim() == 2 and block_tables.stride(1) == 1
+    assert block_tables.size(0) >= B, "block_tables has fewer rows than q"
+    if out is None:
+        out = torch.empty((B, Lq, Hq, D), dtype=q.dtype, device=q.device)
+    else:
+        assert out.shape == (B, Lq, Hq, D) and out.is_contiguous() and out.dtype == q.dtype
+    if workspace is None:
+        workspace = paged_workspace(q.device, Lq, Hq // Hkv, B * Hkv)
+    rc = lib().b200_paged_attention(out.data_ptr(), q.data_ptr(), q_tok, k_cache.data_ptr(), v_cache.data_ptr(), NB, bs, block_tables.data_ptr(),
+                                    block_tables.stride(0), context_lens.data_ptr(), B, Lq, Hq, Hkv, D,
+                                    float(softmax_scale), _DTYPES[q.dtype], workspace.data_ptr(),
+                                    workspace.numel(), _stream(q))
+    check(rc, "paged_attention")
+    return out
+
+
+def flash_attn_with_kvcache(q, k_cache, v_cache, cache_seqlens=None, block_table=None, softmax_scale=None,
+                            causal=True, out=None):
+    """Drop-in for the decode call of nanovllm/layers/attention.py:72-74.
+
+    q [B, Lq, Hq, D], k_cache/v_cache [num_blocks, block_size, Hkv, D],
+    cache_seqlens int32 [B], block_table int32 [B, W]; returns [B, Lq, Hq, D].
+    """
+    assert cache_seqlens is not None and block_table is not None, "the B200 path reads a paged cache"
+    if not causal and q.size(1) > 1:
+        raise NotImplementedError("non-causal multi-query paged attention")
+    scale = q.size(-1) ** -0.5 if softmax_scale is None else softmax_scale
+    return paged_attention(q, k_cache, v_cache, cache_seqlens, block_table, scale, out=out)
+
+
+def workspace_error(workspace: torch.Tensor) -> int:
+    """Device error word of a paged-attention workspace (synchronises)."""
+    flag = ctypes.c_int32(0)
+    check(lib().b200_workspace_error(workspace.data_ptr(), _stream(workspace), ctypes.byref(flag)),
+          "workspace_error")
+    return flag.value
+
+
+# ------------------------------------------------------------ varlen prefill
+def flash_attn_varlen_func(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k, softmax_scale=None,
+                           causal=True, block_table=None, out=None):
+    """Drop-in for the prefill call of nanovllm/layers/attention.py:67-70.
+
+    q [Tq, Hq, D]; k/v packed [Tk, Hkv, D] or, with block_table, the layer's
+    caches [num_blocks, block_size, Hkv, D]; returns [Tq, Hq, D].
+    """
+    if not causal:
+        raise NotImplementedError("non-causal prefill")
+    Tq, Hq, D = q.shape
+    _require_cuda(q, k, v, cu_seqlens_q, cu_seqlens_k)
+    assert q.dtype in _DTYPES and k.dtype == q.dtype == v.dtype, "q/k/v dtype must match (bf16/fp16)"
+    assert q.stride(-1) == 1 and q.stride(-2) == D, "q heads must be contiguous"
+    assert cu_seqlens_q.dtype == torch.int32 and cu_seqlens_k.dtype == torch.int32
+    S = cu_seqlens_q.numel() - 1
+    assert cu_seqlens_k.numel() == S + 1
+    if block_table is not None:
+        NB, bs, Hkv, Dk = k.shape
+        assert k.is_contiguous() and v.is_contiguous() and v.shape == k.shape
+        assert block_table.dtype == torch.int32 and block_table.stride(1) == 1
+        k_stride = v_stride = Hkv * D
+        total_k_rows = NB * bs
+        bt_ptr, bt_stride = block_table.data_ptr(), block_table.stride(0)
+    else:
+        Tk, Hkv, Dk = k.shape
+        assert k.stride(-1) == 1 and k.stride(-2) == D and v.stride(-1) == 1 and v.stride(-2) == D
+        k_stride, v_stride = k.stride(0), v.stride(0)
+        total_k_rows, bs = Tk, 0
+        bt_ptr, bt_stride = None, 0
+    assert Dk == D
+    if out is None:
+        out = torch.empty((Tq, Hq, D), dtype=q.dtype, device=q.device)
+    scale = D ** -0.5 if softmax_scale is None else softmax_scale
+    if Tq == 0 or S == 0:
+        return out
+    rc = lib().b200_varlen_prefill(out.data_ptr(), q.data_ptr(), q.stride(0), k.data_ptr(), k_stride, v.data_ptr(),
+                                   v_stride, cu_seqlens_q.data_ptr(), cu_seqlens_k.data_ptr(), S,
+                                   int(max_seqlen_q), int(max_seqlen_k), total_k_rows, bt_ptr, bt_stride, bs,
+                                   Hq, Hkv, D, float(scale), _DTYPES[q.dtype], _stream(q))
+    check(rc, "varlen_prefill")
+    return out
+
+
+# ------------------------------------------------------ speculative decoding
+def spec_accept(target_logits, draft_logits, draft_tokens, uniform_accept, uniform_sample, temperatures=None,
+                workspace=None):
+    """Rejection-sampling acceptance of k draft tokens per sequence.
+
+    target_logits [B, k+1, V], draft_logits [B, k, V] fp32; draft_tokens,
+    uniform_accept [B, k]; uniform_sample [B]; temperatures [B] or None.
+    Returns (tokens int32 [B, k+1] padded with -1, num_tokens int32 [B]).
+    """
+    B, k1, V = target_logits.shape
+    k = k1 - 1
+    _require_cuda(target_logits, draft_logits, draft_tokens, uniform_accept, uniform_sample)
+    for t in (target_logits, draft_logits, uniform_accept, uniform_sample):
+        assert t.dtype == torch.float32 and t.is_contiguous()
+    assert draft_logits.shape == (B, k, V) and draft_tokens.shape == (B, k) and uniform_accept.shape == (B, k)
+    assert draft_tokens.dtype == torch.int32 and draft_tokens.is_contiguous() and uniform_sample.shape == (B,)
+    if temperatures is not None:
+        assert temperatures.dtype == torch.float32 and temperatures.shape == (B,) and temperatures.is_cuda
+    tokens = torch.empty((B, k1), dtype=torch.int32, device=target_logits.device)
+    num = torch.empty((B,), dtype=torch.int32, device=target_logits.device)
+    need = lib().b200_spec_accept_workspace_size(B, k, V)
+    if workspace is None:
+        workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=target_logits.device)
+    rc = lib().b200_spec_accept(tokens.data_ptr(), num.data_ptr(), target_logits.data_ptr(),
+                                draft_logits.data_ptr(), draft_tokens.data_ptr(), uniform_accept.data_ptr(),
+                                uniform_sample.data_ptr(), None if temperatures is None else temperatures.data_ptr(),
+                                B, k, V, workspace.data_ptr(), workspace.numel(), _stream(target_logits))
+    check(rc, "spec_accept")
+    return tokens, num

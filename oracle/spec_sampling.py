@@ -1,0 +1,217 @@
+"""Speculative acceptance-sampling oracle (test infrastructure only).
+
+The reference engine has no speculative path (nothing under nanovllm/ drafts
+or verifies tokens); its only sampler is the exponential race of
+nanovllm/layers/sampler.py:7-12.  This module restates the standard
+rejection scheme for speculative decoding (Leviathan et al. 2023; Chen et
+al. 2023):
+  for draft position i = 0..k-1 with draft token x_i:
+      accept when u_i < min(1, p_i(x_i) / q_i(x_i))
+  at the first rejection i: sample from normalise(max(p_i - q_i, 0));
+  if all k drafts are accepted: sample a bonus token from p_k,
+with p = softmax(target_logits / T) and q = softmax(draft_logits / T).
+
+Every floating-point operation is defined in a fixed order with float32
+rounding, so that the CUDA kernel reproduces the decisions and the sampled
+tokens bit for bit given identical uniforms:
+  * exp_c: exp(x) = 2^n * P(f) with y = x*log2(e), n = rint(y), f = y - n,
+    P the degree-7 Taylor polynomial of 2^f (coefficients ln2^k / k!),
+    Horner with separate multiply and add, 0 below y = -125;
+  * sums: the vocabulary is cut into tiles of 4096; in a tile, "thread" i
+    (0..255) adds its 16 elements k*1024 + 4*i + c (k = 0..3 outer,
+    c = 0..3 inner) left to right; the 32 thread sums of each warp are
+    combined by an xor butterfly (16, 8, 4, 2, 1); the 8 warp sums are
+    added left to right; tile sums are added left to right;
+  * sampling: inverse CDF over the same hierarchy (tile sums, then thread
+    sums, then the thread's 16 elements), each level scanned left to right
+    with float32 running sums; a level where rounding leaves the target
+    above the running sum falls back to its last positive entry.
+"""
+import math
+import numpy as np
+
+f32 = np.float32
+TILE = 4096
+THREADS = 256
+LOG2E = f32(1.4426950408889634)
+# 2^f = sum_k (f ln2)^k / k!  ->  coefficients ln2^k / k!, rounded to float32
+EXP2_COEF = [f32(math.log(2.0) ** k / math.factorial(k)) for k in range(8)]
+
+
+def exp_c(x):
+    """exp(x) for float32 x <= ~87 with the fixed operation order above."""
+    x = np.asarray(x, dtype=f32)
+    y = (x * LOG2E).astype(f32)
+    n = np.rint(y).astype(f32)
+    fr = (y - n).astype(f32)
+    p = np.full_like(fr, EXP2_COEF[7])
+    for c in EXP2_COEF[6::-1]:
+        p = (p * fr).astype(f32)
+        p = (p + c).astype(f32)
+    ni = np.clip(n, -126, 127).astype(np.int32)
+    scale = ((ni + 127).astype(np.uint32) << np.uint32(23)).view(f32)
+    r = (p * scale).astype(f32)
+    return np.where(y < f32(-125.0), f32(0.0), r).astype(f32)
+
+
+def exp2_coef_hex():
+    """The float32 coefficients as C hex literals (the CUDA kernel's constants)."""
+    return [float(c).hex() for c in EXP2_COEF]
+
+
+def canon_partials(w):
+    """Thread sums P[..., T, 256], tile sums S[..., T] and total R[...] of w[..., V]."""
+    w = np.asarray(w, dtype=f32)
+    V = w.shape[-1]
+    T = (V + TILE - 1) // TILE
+    pad = np.zeros(w.shape[:-1] + (T * TILE,), f32)
+    pad[..., :V] = w
+    X = pad.reshape(w.shape[:-1] + (T, 4, THREADS, 4))
+    P = np.zeros(w.shape[:-1] + (T, THREADS), f32)
+    for k in range(4):
+        for c in range(4):
+            P = (P + X[..., k, :, c]).astype(f32)
+    B2 = P.reshape(w.shape[:-1] + (T, THREADS // 32, 32))
+    lanes = np.arange(32)
+    for off in (16, 8, 4, 2, 1):
+        B2 = (B2 + B2[..., lanes ^ off]).astype(f32)
+    W = B2[..., 0]
+    S = np.zeros(w.shape[:-1] + (T,), f32)
+    for wi in range(THREADS // 32):
+        S = (S + W[..., wi]).astype(f32)
+    R = np.zeros(w.shape[:-1], f32)
+    for t in range(T):
+        R = (R + S[..., t]).astype(f32)
+    return P, S, R
+
+
+def _scan_pick(vals, target, acc0):
+    """Left-to-right running sum from acc0; first index with target < acc + v.
+
+    Returns (index, running sum before it) or the last positive entry when
+    rounding leaves the target above every running sum; (-1, acc0) if no
+    entry is positive.
+    """
+    acc = f32(acc0)
+    for i, v in enumerate(vals):
+        nxt = f32(acc + f32(v))
+        if target < nxt and v > 0:
+            return i, acc
+        acc = nxt
+    acc = f32(acc0)
+    last, acc_last = -1, f32(acc0)
+    for i, v in enumerate(vals):
+        if v > 0:
+            last, acc_last = i, acc
+        acc = f32(acc + f32(v))
+    return last, acc_last
+
+
+def canon_pick(w, u):
+    """Index sampled from weights w[V] >= 0 with uniform u, or -1 if w has no mass."""
+    w = np.asarray(w, dtype=f32)
+    V = w.shape[-1]
+    P, S, R = canon_partials(w)
+    target = f32(f32(u) * R)
+    t, acc = _scan_pick(S, target, f32(0.0))
+    if t < 0:
+        return -1
+    i, acc = _scan_pick(P[t], target, acc)
+    if i < 0:
+        return -1
+    idx = [t * TILE + k * 1024 + 4 * i + c for k in range(4) for c in range(4)]
+    vals = [w[j] if j < V else f32(0.0) for j in idx]
+    e, _ = _scan_pick(vals, target, acc)
+    return -1 if e < 0 else idx[e]
+
+
+def scaled_logits(logits, temperature):
+    x = np.asarray(logits, dtype=f32)
+    if temperature is None:
+        return x
+    return (x / f32(temperature)).astype(f32)
+
+
+def row_stats(x):
+    """(max, canonical sum of exp_c(x - max)) of one logits row (already / T)."""
+    M = f32(x.max())
+    e = exp_c((x - M).astype(f32))
+    _, _, R = canon_partials(e)
+    return M, f32(R)
+
+
+def probs(x, M, S):
+    return (exp_c((x - M).astype(f32)) / S).astype(f32)
+
+
+def spec_accept_ref(target_logits, draft_logits, draft_tokens, u_accept, u_sample,
+                    temperatures=None):
+    """Returns (tokens [B, k+1] int32 padded with -1, num_tokens [B] int32)."""
+    tl = np.asarray(target_logits, f32)
+    dl = np.asarray(draft_logits, f32)
+    B, k1, V = tl.shape
+    k = k1 - 1
+    tokens = np.full((B, k1), -1, np.int32)
+    num = np.zeros(B, np.int32)
+    for b in range(B):
+        T = None if temperatures is None else temperatures[b]
+        rej = k
+        for i in range(k):
+            x = int(draft_tokens[b, i])
+            if not (0 <= x < V):
+                rej = i
+                break
+            xt = scaled_logits(tl[b, i], T)
+            xd = scaled_logits(dl[b, i], T)
+            Mt, St = row_stats(xt)
+            Md, Sd = row_stats(xd)
+            p = f32(exp_c(f32(xt[x] - Mt)) / St)
+            q = f32(exp_c(f32(xd[x] - Md)) / Sd)
+            if q > 0:
+                acc = f32(u_accept[b, i]) < min(f32(1.0), f32(p / q))
+            else:
+                acc = p > 0
+            if not acc:
+                rej = i
+                break
+        xt = scaled_logits(tl[b, rej], T)
+        Mt, St = row_stats(xt)
+        p_row = probs(xt, Mt, St)
+        if rej < k:
+            xd = scaled_logits(dl[b, rej], T)
+            Md, Sd = row_stats(xd)
+            q_row = probs(xd, Md, Sd)
+            w = np.maximum((p_row - q_row).astype(f32), f32(0.0))
+            tok = canon_pick(w, u_sample[b])
+            if tok < 0:
+                tok = canon_pick(p_row, u_sample[b])
+        else:
+            tok = canon_pick(p_row, u_sample[b])
+        if tok < 0:
+            tok = 0
+        tokens[b, :rej] = draft_tokens[b, :rej]
+        tokens[b, rej] = tok
+        num[b] = rej + 1
+    return tokens, num
+
+
+def spec_accept_float_ref(target_logits, draft_logits, draft_tokens, u_accept):
+    """Acceptance count from float64 softmax: a sanity check of the scheme itself."""
+    tl = np.asarray(target_logits, np.float64)
+    dl = np.asarray(draft_logits, np.float64)
+    p = np.exp(tl - tl.max(-1, keepdims=True))
+    p /= p.sum(-1, keepdims=True)
+    q = np.exp(dl - dl.max(-1, keepdims=True))
+    q /= q.sum(-1, keepdims=True)
+    B, k = draft_tokens.shape
+    out = np.zeros(B, np.int32)
+    for b in range(B):
+        n = 0
+        for i in range(k):
+            x = draft_tokens[b, i]
+            if u_accept[b, i] < min(1.0, p[b, i, x] / q[b, i, x]):
+                n += 1
+            else:
+                break
+        out[b] = n
+    return out

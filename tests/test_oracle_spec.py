@@ -1,0 +1,72 @@
+"""Speculative acceptance oracle: fixed-order arithmetic and scheme sanity (CPU)."""
+import numpy as np
+import pytest
+
+from oracle import cases
+from oracle import spec_sampling as ss
+
+
+def test_exp_c_accuracy():
+    x = np.linspace(-80, 0, 200001).astype(np.float32)
+    rel = np.abs(ss.exp_c(x) - np.exp(x.astype(np.float64))) / np.exp(x.astype(np.float64))
+    assert rel.max() < 1e-5
+    assert ss.exp_c(np.float32(-100.0)) == 0 and ss.exp_c(np.float32(0.0)) == 1.0
+
+
+def test_canonical_sum_close_to_exact():
+    rng = np.random.default_rng(0)
+    for V in (1, 4095, 4096, 4097, 151936):
+        w = rng.random(V, dtype=np.float32)
+        _, S, R = ss.canon_partials(w)
+        assert len(S) == (V + 4095) // 4096
+        assert abs(float(R) - w.astype(np.float64).sum()) <= 1e-5 * w.sum()
+
+
+def test_canonical_pick_follows_the_cdf():
+    w = np.zeros(9000, np.float32)
+    w[[3, 4100, 8999]] = [1.0, 2.0, 1.0]
+    picks = [ss.canon_pick(w, u) for u in (0.0, 0.2, 0.26, 0.6, 0.74, 0.76, 0.999)]
+    assert picks == [3, 3, 4100, 4100, 4100, 8999, 8999]
+    assert ss.canon_pick(np.zeros(10, np.float32), 0.5) == -1
+
+
+def test_canonical_pick_distribution():
+    rng = np.random.default_rng(1)
+    w = rng.random(300, dtype=np.float32) ** 4
+    us = rng.random(20000, dtype=np.float32)
+    counts = np.bincount([ss.canon_pick(w, u) for u in us], minlength=300)
+    p = w / w.sum()
+    assert np.abs(counts / len(us) - p).max() < 0.01
+
+
+def test_acceptance_counts_match_float64_scheme():
+    c = cases.make_spec_case(64, 4, 1000, seed=3)
+    toks, num = ss.spec_accept_ref(c.target_logits, c.draft_logits, c.draft_tokens, c.u_accept, c.u_sample)
+    ref = ss.spec_accept_float_ref(c.target_logits, c.draft_logits, c.draft_tokens, c.u_accept)
+    assert (num - 1 == ref).mean() > 0.98          # only near-ties may differ
+    assert 0 < (num - 1).mean() < 4                # both branches are exercised
+    for b in range(64):
+        n = num[b]
+        assert (toks[b, :n - 1] == c.draft_tokens[b, :n - 1]).all()
+        assert 0 <= toks[b, n - 1] < 1000 and (toks[b, n:] == -1).all()
+
+
+def test_rejected_position_never_resamples_the_rejected_mass():
+    """After a rejection at i the new token has p_i(x) > q_i(x) (residual support)."""
+    c = cases.make_spec_case(32, 3, 500, seed=4)
+    toks, num = ss.spec_accept_ref(c.target_logits, c.draft_logits, c.draft_tokens, c.u_accept, c.u_sample)
+    for b in range(32):
+        i = num[b] - 1
+        if i < 3:
+            xt, xd = c.target_logits[b, i], c.draft_logits[b, i]
+            p = ss.probs(xt, *ss.row_stats(xt))
+            q = ss.probs(xd, *ss.row_stats(xd))
+            assert p[toks[b, i]] > q[toks[b, i]]
+
+
+def test_temperature_and_invalid_draft():
+    c = cases.make_spec_case(4, 2, 300, seed=5, temperatures=True)
+    c.draft_tokens[1, 0] = 300  # out of range -> rejected at position 0
+    toks, num = ss.spec_accept_ref(c.target_logits, c.draft_logits, c.draft_tokens, c.u_accept, c.u_sample,
+                                   c.temperatures)
+    assert num[1] == 1 and 0 <= toks[1, 0] < 300

@@ -1,0 +1,44 @@
+"""Speculative acceptance sampling on the GPU vs the oracle: decisions and
+sampled tokens bit-exact given identical uniforms."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import cases
+from oracle import spec_sampling as ss
+
+pytestmark = pytest.mark.gpu
+
+
+def run(pkg, c):
+    t = lambda x: torch.from_numpy(np.ascontiguousarray(x)).cuda()
+    temps = None if c.temperatures is None else t(c.temperatures)
+    toks, num = pkg.spec_accept(t(c.target_logits), t(c.draft_logits), t(c.draft_tokens), t(c.u_accept),
+                                t(c.u_sample), temps)
+    want_t, want_n = ss.spec_accept_ref(c.target_logits, c.draft_logits, c.draft_tokens, c.u_accept, c.u_sample,
+                                        c.temperatures)
+    return toks.cpu().numpy(), num.cpu().numpy(), want_t, want_n
+
+
+@pytest.mark.parametrize("B,k,V,seed", [(16, 4, 1000, 0), (8, 4, 4096, 1), (8, 2, 4097, 2), (4, 4, 151936, 3),
+                                        (32, 1, 777, 4), (3, 6, 20000, 5)])
+def test_bit_exact_against_oracle(pkg, B, k, V, seed):
+    c = cases.make_spec_case(B, k, V, seed=seed)
+    toks, num, wt, wn = run(pkg, c)
+    assert np.array_equal(num, wn) and np.array_equal(toks, wt)
+
+
+def test_temperatures_and_invalid_drafts(pkg):
+    c = cases.make_spec_case(8, 3, 3000, seed=9, temperatures=True)
+    c.draft_tokens[2, 1] = -5
+    c.draft_tokens[5, 0] = 3000
+    toks, num, wt, wn = run(pkg, c)
+    assert np.array_equal(num, wn) and np.array_equal(toks, wt)
+    assert num[5] == 1
+
+
+def test_uncorrelated_drafts_mostly_rejected(pkg):
+    c = cases.make_spec_case(16, 4, 2000, seed=10, correlated=False)
+    toks, num, wt, wn = run(pkg, c)
+    assert np.array_equal(num, wn) and np.array_equal(toks, wt)
+    assert num.mean() < 2
