@@ -176,3 +176,13 @@ def test_config5_sampled_rows_and_determinism(pkg):
         want = oatt.paged_attention_ref(qn[b:b + 1], Kp, Vp, np.arange(len(blocks), dtype=np.int32)[None],
                                         ctx[b:b + 1], 128 ** -0.5)
         assert_attn_close(host(o1[b:b + 1]), want, f"config5 row {b} ctx {ctx[b]}")
+
+
+@pytest.mark.parametrize("name", ["decode_config1", "decode_16_4", "decode_32_8", "verify_5"])
+def test_against_flash_attn_golden(pkg, name):
+    """Our kernel vs flash-attn 2.8.3's output on the same inputs (fixture from a B200)."""
+    from tests.test_oracle_golden import golden_case
+    kind, c, q, k, v, want, _ = golden_case(name)
+    out = pkg.paged_attention(dev_bf16(q), dev_bf16(k), dev_bf16(v), dev_i32(c.context_lens),
+                              dev_i32(c.block_tables), c.scale)
+    assert_attn_close(host(out), want.reshape(q.shape), name)
