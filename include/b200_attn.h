@@ -107,6 +107,31 @@ B200_API int32_t b200_paged_attention(void* out, const void* q, int64_t q_stride
                              void* stream);
 
 /*
+ * Allocation-free variant of b200_paged_attention; no counterpart in the
+ * reference (which always has PyTorch's allocator at hand).  For callers that
+ * cannot allocate device memory on the execution path -- runtimes whose own
+ * allocator owns the device heap and gives plugins no workspace, plugin hosts
+ * that forbid cudaMalloc there, code that must not risk cudaMalloc/cudaFree's
+ * implicit device synchronisation.  Same arguments and results as
+ * b200_paged_attention without the workspace: the split-K scratch is a 32 MiB
+ * array inside the library that every GPU loading the library holds until the
+ * process exits.  Limit: batch * num_kv_heads <= 8192 and at most
+ * (32 MiB - 33 KiB) / (query_len * Hq/Hkv * 516 B) work items; larger calls
+ * return B200_ERR_WORKSPACE.  The first call on a device looks up the array's
+ * device address (make it before any stream capture).  Calls share the array:
+ * each clears the control words it needs, and calls that overlap on the GPU
+ * race, so serialise them.
+ */
+B200_API int32_t b200_paged_attention_noalloc(void* out, const void* q, int64_t q_stride_token,
+                                     const void* k_cache, const void* v_cache,
+                                     int32_t num_blocks, int32_t block_size,
+                                     const int32_t* block_tables, int32_t block_table_stride,
+                                     const int32_t* context_lens, int32_t batch,
+                                     int32_t query_len, int32_t num_heads,
+                                     int32_t num_kv_heads, int32_t head_dim,
+                                     float softmax_scale, int32_t dtype, void* stream);
+
+/*
  * Copies the workspace's device-side error word to *flag (synchronously on
  * `stream`).  Non-zero means a bounded wait inside a kernel gave up; the
  * results of that call are undefined.  For tests and diagnostics only.

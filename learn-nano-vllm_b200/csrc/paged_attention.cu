@@ -25,6 +25,7 @@
 // reductions; the four partial states are combined through shared memory at
 // the end of an item.
 #include <climits>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -586,6 +587,165 @@ extern "C" int32_t b200_paged_attention(void* out, const void* q, int64_t q_stri
         fn = hi ? (const void*)paged_attention_kernel<false, true> : (const void*)paged_attention_kernel<false, false>;
     }
     smem = hi ? smem_bytes<16>() : smem_bytes<8>();
+    ensure_smem_attr(fn, smem);
+    if (bf16) {
+        if (hi) paged_attention_kernel<true, true><<<grid, block, smem, s>>>(prm, tmk, tmv);
+        else paged_attention_kernel<true, false><<<grid, block, smem, s>>>(prm, tmk, tmv);
+    } else {
+        if (hi) paged_attention_kernel<false, true><<<grid, block, smem, s>>>(prm, tmk, tmv);
+        else paged_attention_kernel<false, false><<<grid, block, smem, s>>>(prm, tmk, tmv);
+    }
+    B200_CUDA_TRY(cudaGetLastError());
+    return B200_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of b200_paged_attention.
+//
+// Some callers cannot call cudaMalloc around an attention call: inference
+// runtimes whose own allocator owns the whole device heap and hands plugins
+// no workspace, plugin hosts that forbid device allocation on the execution
+// path, and code that must not risk the implicit device synchronisation of
+// cudaMalloc/cudaFree.  For them this entry point keeps the split-K scratch
+// (control block, split counters, partial outputs) in a file-scope device
+// array of kNoAllocScratchBytes.  Every GPU that loads this library holds
+// that array until the process exits.  The array's host-side name is only a
+// stand-in for the symbol, so the first call on each device looks up its
+// device address with cudaGetSymbolAddress (with that device current) and
+// caches it; make that first call before any stream capture.  All calls
+// share the one array and it keeps the last call's contents: each call
+// clears the control words and split counters it uses before launching,
+// and calls that overlap on the GPU (two streams, two host threads) race
+// on it and must be serialised by the caller.
+namespace b200 {
+namespace pa {
+
+constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;  // 32 MiB per device
+constexpr int kNoAllocCounterSlots = 8192;                  // (sequence, kv head) pairs
+constexpr size_t kNoAllocFixedBytes = kCtrlWords * 4 + size_t(kNoAllocCounterSlots) * 4;
+
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on the current device (looked up once per device).
+int32_t noalloc_scratch(void** out) {
+    int dev = 0;
+    B200_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kNoAllocMaxDevices)
+        return fail(B200_ERR_UNSUPPORTED, "paged_attention_noalloc: device %d beyond %d", dev, kNoAllocMaxDevices);
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (g_noalloc_ptr[dev] == nullptr) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || p == nullptr)
+            return fail(B200_ERR_CUDA, "paged_attention_noalloc: cudaGetSymbolAddress failed: %s",
+                        cudaGetErrorString(e));
+        g_noalloc_ptr[dev] = p;
+    }
+    *out = g_noalloc_ptr[dev];
+    return B200_OK;
+}
+}  // namespace
+
+}  // namespace pa
+}  // namespace b200
+
+extern "C" int32_t b200_paged_attention_noalloc(void* out, const void* q, int64_t q_stride_token,
+                                                const void* k_cache, const void* v_cache, int32_t num_blocks,
+                                                int32_t block_size, const int32_t* block_tables,
+                                                int32_t block_table_stride, const int32_t* context_lens,
+                                                int32_t batch, int32_t query_len, int32_t num_heads,
+                                                int32_t num_kv_heads, int32_t head_dim, float softmax_scale,
+                                                int32_t dtype, void* stream) {
+    using namespace b200;
+    using namespace b200::pa;
+    clear_error();
+    B200_REQUIRE(batch >= 0, "paged_attention_noalloc: batch %d < 0", batch);
+    if (batch == 0) return B200_OK;
+    B200_REQUIRE(out && q && k_cache && v_cache && block_tables && context_lens,
+                 "paged_attention_noalloc: null pointer");
+    B200_REQUIRE(num_heads > 0 && num_kv_heads > 0 && num_heads % num_kv_heads == 0,
+                 "paged_attention_noalloc: num_heads %d not a multiple of num_kv_heads %d", num_heads, num_kv_heads);
+    B200_REQUIRE(query_len >= 1, "paged_attention_noalloc: query_len %d < 1", query_len);
+    const int group = num_heads / num_kv_heads;
+    const int rows = query_len * group;
+    if (head_dim != kD) return fail(B200_ERR_UNSUPPORTED, "paged_attention_noalloc: head_dim %d (only 128)", head_dim);
+    if (rows > 16)
+        return fail(B200_ERR_UNSUPPORTED, "paged_attention_noalloc: query_len * Hq/Hkv = %d exceeds 16", rows);
+    if (dtype != B200_BF16 && dtype != B200_F16)
+        return fail(B200_ERR_UNSUPPORTED, "paged_attention_noalloc: dtype %d (bf16 or fp16 only)", dtype);
+    if (batch > kMaxBatch)
+        return fail(B200_ERR_UNSUPPORTED, "paged_attention_noalloc: batch %d > %d", batch, kMaxBatch);
+    B200_REQUIRE(block_size > 0 && block_size % kTile == 0,
+                 "paged_attention_noalloc: block_size %d not a multiple of %d", block_size, kTile);
+    B200_REQUIRE(num_blocks > 0 && int64_t(num_blocks) * block_size < (int64_t(1) << 31),
+                 "paged_attention_noalloc: num_blocks %d out of range", num_blocks);
+    B200_REQUIRE(block_table_stride > 0 && int64_t(block_table_stride) * block_size < (int64_t(1) << 31),
+                 "paged_attention_noalloc: block_table_stride %d out of range", block_table_stride);
+    B200_REQUIRE(q_stride_token >= int64_t(num_heads) * head_dim && q_stride_token % 2 == 0,
+                 "paged_attention_noalloc: q token stride %lld", (long long)q_stride_token);
+    B200_REQUIRE((reinterpret_cast<uintptr_t>(q) & 3) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0,
+                 "paged_attention_noalloc: q must be 4-byte and out 16-byte aligned");
+    const int64_t pairs = int64_t(batch) * num_kv_heads;
+    const int64_t max_items = int64_t(kNoAllocScratchBytes - kNoAllocFixedBytes) / (int64_t(rows) * (kD + 1) * 4);
+    if (pairs > kNoAllocCounterSlots || pairs > max_items)
+        return fail(B200_ERR_WORKSPACE,
+                    "paged_attention_noalloc: batch * num_kv_heads = %lld exceeds the built-in %zu-byte scratch "
+                    "(at most %lld pairs for query_len * Hq/Hkv = %d); use b200_paged_attention with a workspace",
+                    (long long)pairs, kNoAllocScratchBytes,
+                    (long long)(max_items < kNoAllocCounterSlots ? max_items : kNoAllocCounterSlots), rows);
+
+    void* scratch = nullptr;
+    int32_t rc = noalloc_scratch(&scratch);
+    if (rc) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // Control block (scheduler, finished CTAs, error word) and this call's split counters start at zero.
+    B200_CUDA_TRY(cudaMemsetAsync(scratch, 0, kCtrlWords * 4 + size_t(pairs) * 4, s));
+
+    const bool bf16 = dtype == B200_BF16;
+    const uint64_t row_elems = uint64_t(num_kv_heads) * kD;
+    const uint64_t rows_total = uint64_t(num_blocks) * block_size;
+    CUtensorMap tmk, tmv;
+    rc = make_tmap_2d(&tmk, k_cache, row_elems, rows_total, row_elems * 2, 64, kTile, bf16, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    rc = make_tmap_2d(&tmv, v_cache, row_elems, rows_total, row_elems * 2, 64, kTile, bf16, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+
+    Params prm;
+    prm.q = static_cast<const uint16_t*>(q);
+    prm.q_stride = q_stride_token;
+    prm.out = static_cast<uint16_t*>(out);
+    prm.block_tables = block_tables;
+    prm.bt_stride = block_table_stride;
+    prm.context_lens = context_lens;
+    prm.batch = batch;
+    prm.lq = query_len;
+    prm.hq = num_heads;
+    prm.hkv = num_kv_heads;
+    prm.group = group;
+    prm.rows = rows;
+    prm.block_size = block_size;
+    prm.num_blocks = num_blocks;
+    prm.scale_log2 = softmax_scale * 1.4426950408889634f;
+    char* ws = static_cast<char*>(scratch);
+    prm.ctrl = reinterpret_cast<int32_t*>(ws);
+    prm.counters = reinterpret_cast<int32_t*>(ws + kCtrlWords * 4);
+    prm.part_o = reinterpret_cast<float*>(ws + kNoAllocFixedBytes);
+    prm.part_lse = prm.part_o + max_items * rows * kD;
+    prm.max_items = int32_t(max_items);
+
+    const dim3 grid(device_sm_count()), block(kThreads);
+    const bool hi = rows > 8;
+    const void* fn;
+    if (bf16)
+        fn = hi ? (const void*)paged_attention_kernel<true, true> : (const void*)paged_attention_kernel<true, false>;
+    else
+        fn = hi ? (const void*)paged_attention_kernel<false, true> : (const void*)paged_attention_kernel<false, false>;
+    const int smem = hi ? smem_bytes<16>() : smem_bytes<8>();
     ensure_smem_attr(fn, smem);
     if (bf16) {
         if (hi) paged_attention_kernel<true, true><<<grid, block, smem, s>>>(prm, tmk, tmv);
