@@ -53,12 +53,14 @@ def parse():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--batch", type=int, default=BATCH,
+                    help="sequences in the batch (profiling runs use a smaller batch; the bench line uses 512)")
     return ap.parse_args()
 
 
-def workload():
+def workload(batch=BATCH):
     from oracle.cases import config5_context_lens
-    ctx = config5_context_lens(BATCH, SIGMA, seed=0, cap=CAP)
+    ctx = config5_context_lens(batch, SIGMA, seed=0, cap=CAP)
     return ctx
 
 
@@ -242,7 +244,7 @@ def run_reference(args, rank, world):
 
 def config_dict(world, ctx):
     return {"workload": "config5: Qwen3-8B attention layer decode (store_kvcache + paged attention)",
-            "batch": BATCH, "q_heads": HQ_TOTAL, "kv_heads": HKV_TOTAL, "head_dim": HEAD_DIM, "block_size": BLOCK,
+            "batch": len(ctx), "q_heads": HQ_TOTAL, "kv_heads": HKV_TOTAL, "head_dim": HEAD_DIM, "block_size": BLOCK,
             "context_lens": f"lognormal(ln 2048, {SIGMA}) capped {CAP}, seed 0", "sum_ctx": int(ctx.sum()),
             "parallelism": f"tp{world} (kv-head sharded)",
             "l2": "no flush: per-step KV bytes per rank >> 126 MB L2"}
@@ -270,7 +272,8 @@ def main():
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
-    ctx = workload()
+    ctx = workload(args.batch)
+    BATCH = len(ctx)
     hq, hkv = HQ_TOTAL // world, HKV_TOTAL // world
     nblk = (ctx + BLOCK - 1) // BLOCK
     nb = int(nblk.sum())

@@ -79,8 +79,9 @@ B200_API int32_t b200_store_kvcache(const void* key, int64_t key_stride,
  *                             cache_seqlens=context_lens,
  *                             block_table=block_tables,
  *                             softmax_scale=scale, causal=True)
- * q   : [batch, query_len, Hq, D], token stride q_stride_token
- * out : [batch, query_len, Hq, D] contiguous, same dtype as q
+ * q   : [batch, query_len, Hq, D], token stride q_stride_token (a multiple
+ *       of 8 elements), 16-byte aligned
+ * out : [batch, query_len, Hq, D] contiguous, 16-byte aligned, dtype of q
  * context_lens[b] counts every cached token of sequence b including its
  * query_len new ones; query j of sequence b sees cache positions
  * p <= context_lens[b] - query_len + j (causal, bottom-right aligned).
@@ -89,8 +90,8 @@ B200_API int32_t b200_store_kvcache(const void* key, int64_t key_stride,
  * workspace: b200_paged_attention_workspace_size() bytes, 256-byte aligned,
  * zero-filled once before the first call; every call leaves its control
  * region zeroed again.  Calls sharing a workspace must not overlap on the GPU.
- * Constraints: D == 128, dtype bf16 or fp16, block_size % 64 == 0,
- * batch <= 4096, query_len * (Hq / Hkv) <= 16.
+ * Constraints: D == 128, dtype bf16 or fp16, block_size % 128 == 0,
+ * batch <= 2048, query_len * (Hq / Hkv) <= 16.
  */
 B200_API size_t b200_paged_attention_workspace_size(int32_t max_items, int32_t query_len,
                                            int32_t group_size, int32_t head_dim);

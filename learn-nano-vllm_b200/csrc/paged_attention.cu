@@ -3,27 +3,34 @@
 // nanovllm/layers/attention.py:71-74.
 //
 // Work decomposition.  A work item is (sequence b, kv head h, chunk c): up to
-// kChunkMaxTiles tiles of 64 cached tokens of one kv head.  All Lq*G query
-// rows that read kv head h (G = Hq/Hkv query heads times Lq queries, at most
-// 16) are processed together, so every K/V byte is read from HBM once.  The
+// `chunk` tiles of 128 cached tokens of one kv head.  All Lq*G query rows
+// that read kv head h (G = Hq/Hkv query heads times Lq queries, at most 16)
+// are processed together, so every K/V byte is read from HBM once.  The
 // chunking is planned on the device from context_lens (no host sync, so the
 // call is CUDA-graph capturable): every CTA scans context_lens into shared
-// memory, picks a chunk length that gives ~kWaves items per CTA, and claims
-// items dynamically from an atomic counter in the workspace.  Items of a
+// memory and picks the chunk length (about kWaves items per CTA, at most
+// kChunkMaxTiles tiles, and coarse enough that the items fit the workspace).
+// Items are numbered full-length chunks first, then each sequence's shorter
+// last chunk, and are claimed dynamically from an atomic counter, so that
+// the large items start early and the tail is made of small ones.  Items of a
 // sequence that was split write normalised partial outputs plus their
 // log-sum-exp to the workspace; the CTA that finishes the last chunk of a
 // (b, h) merges them (threadfence-reduction pattern) and writes the output.
 //
-// CTA layout: one persistent CTA per SM, 5 warps.  Warp 4 is the producer:
-// one lane issues 2-D TMA loads (no multicast) of 64x64-element boxes with
-// 128-byte swizzle into a kStages-deep ring of 32 KiB stages (K lo/hi dims,
-// V lo/hi dims) guarded by full/empty mbarriers, and writes a small header
-// per stage describing the tile.  Warps 0-3 are consumers: each takes 16 of
-// the 64 tokens of a stage, computes S = Q K^T and O += P V with
-// mma.sync.m16n8k16 (rows = query rows, padded to 16), and keeps its own
-// online-softmax state (max, sum, O) in registers with warp-shuffle row
-// reductions; the four partial states are combined through shared memory at
-// the end of an item.
+// CTA layout: one persistent CTA per SM, 9 warps.  Warp 8 is the producer:
+// one lane issues 2-D TMA loads (no multicast) of 64-dim x 128-token boxes
+// with 128-byte swizzle into a ring of 64 KiB stages (K lo/hi dims, V lo/hi
+// dims; 3 stages, 2 for more than 8 query rows) guarded by full/empty
+// mbarriers, writes a small header per stage describing the tile, and with
+// an item's first tile bulk-copies its query rows into shared memory.  It
+// fetches the next item's metadata (context length, block ids) while the
+// current item streams.  Warps 0-7 are consumers (two per SM sub-partition,
+// so that one hides the other's latency): each takes 16 of the 128 tokens of
+// a stage, computes S = Q K^T and O += P V with mma.sync.m16n8k16 (rows =
+// query rows, padded to 16), and keeps its own online-softmax state (max,
+// sum, O) in registers with warp-shuffle row reductions; the eight partial
+// states are combined through shared memory at the end of an item (8 -> 4
+// in registers, then 4 -> 1).
 #include <climits>
 #include <mutex>
 
@@ -32,24 +39,24 @@
 namespace b200 {
 namespace pa {
 
-constexpr int kTile = 64;
+constexpr int kTile = 128;                   // tokens per stage
 constexpr int kD = 128;
-constexpr int kStages = 5;
-constexpr int kConsumerWarps = 4;
+constexpr int kConsumerWarps = 8;
 constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kThreads = kConsumers + 32;
-constexpr int kHalfBytes = kTile * 128;      // 64 tokens x 64 dims x 2 B
+constexpr int kHalfBytes = kTile * 128;      // 128 tokens x 64 dims x 2 B
 constexpr int kStageBytes = 4 * kHalfBytes;  // K dims 0-63, K 64-127, V 0-63, V 64-127
-constexpr int kMaxBatch = 4096;
+constexpr int kMaxBatch = 2048;
 constexpr int kCounterSlots = 65536;
 constexpr int kCtrlWords = 64;               // [0] next item, [1] finished CTAs, [2] error word
 constexpr size_t kFixedBytes = kCtrlWords * 4 + size_t(kCounterSlots) * 4;
-constexpr int kWaves = 4;
-constexpr int kChunkMaxTiles = 8;
+constexpr int kWaves = 8;
+constexpr int kChunkMaxTiles = 16;           // at most 2048 tokens per item
 constexpr int kSplitBarrier = 1;             // named barrier of the consumer warps
+constexpr int kRemBits = 12;                 // packed offsets: full-chunk offset << 12 | remainder offset
 
 struct Header {
-    int32_t item, b, h, tile, flags, ctx, nchunks, chunk;
+    int32_t item, b, h, tile, flags, ctx, nchunks, slot0;
 };
 enum : int32_t { kFirst = 1, kLast = 2 };
 
@@ -69,25 +76,32 @@ struct Params {
     int32_t max_items;
 };
 
-template <int RC>
+template <int RC, int NS>
 struct Smem {
-    uint8_t stages[kStages][kStageBytes];
-    float co[kConsumerWarps][RC][kD];
+    uint8_t stages[NS][kStageBytes];
+    uint8_t qbuf[NS][RC * kD * 2];  // query rows of an item, filled with its first tile
+    float co[kConsumerWarps / 2][RC][kD];
     float cm[kConsumerWarps][RC];
     float cl[kConsumerWarps][RC];
-    Header hdr[kStages];
-    uint64_t full[kStages];
-    uint64_t empty[kStages];
-    int32_t chunk_off[kMaxBatch + 1];
+    Header hdr[NS];
+    uint64_t full[NS];
+    uint64_t empty[NS];
+    int32_t off[kMaxBatch + 1];     // (full-chunk offset << kRemBits) | remainder offset
     int32_t red[kThreads / 32 + 1];
     int32_t flag;
     int32_t err;
 };
 
-template <int RC>
-constexpr int smem_bytes() {
-    return int(sizeof(Smem<RC>)) + 1024;
+template <bool ROWS_HI>
+constexpr int num_stages() {
+    return ROWS_HI ? 2 : 3;
 }
+
+template <bool ROWS_HI>
+constexpr int smem_bytes() {
+    return int(sizeof(Smem<ROWS_HI ? 16 : 8, num_stages<ROWS_HI>()>)) + 1024;
+}
+static_assert(smem_bytes<false>() <= 232448 && smem_bytes<true>() <= 232448, "shared memory over 227 KB");
 
 // Block-wide exclusive scan of one int per thread; returns the exclusive
 // prefix and writes the total to *total.  Uses red[] (one slot per warp).
@@ -112,17 +126,80 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* red, int* total)
     return base + x - v;
 }
 
+// Chunk layout of one sequence: nt tiles cut into `full` chunks of `chunk`
+// tiles and, if nt is not a multiple, one shorter remainder chunk.
+struct SeqChunks {
+    int nt, full, rem;
+};
+
+__device__ __forceinline__ SeqChunks seq_chunks(int ctx, int cap, int64_t chunk) {
+    ctx = min(ctx, cap);
+    SeqChunks s;
+    s.nt = ctx > 0 ? (ctx + kTile - 1) / kTile : 0;
+    s.full = int(s.nt / chunk);
+    s.rem = (s.nt - int64_t(s.full) * chunk) > 0 ? 1 : 0;
+    return s;
+}
+
+// Metadata of one claimed work item.  The producer fetches it one item
+// ahead, so that its dependent global loads (context length, block ids)
+// overlap the TMA traffic of the current item.
+constexpr int kPrefetchPages = 4;
+struct ItemMeta {
+    int item, b, h, c, nchunks, ctx, t0, slot0, page0;
+    int blk[kPrefetchPages];
+};
+
+// Partial-output slot (chunk index, before the x Hkv + h) of chunk c of
+// sequence b: full chunks are numbered first, remainder chunks after them.
+__device__ __forceinline__ int chunk_slot(int packed_off, int c, int full, int total_full) {
+    return c < full ? (packed_off >> kRemBits) + c : total_full + (packed_off & ((1 << kRemBits) - 1));
+}
+
+__device__ __forceinline__ void fetch_meta(ItemMeta& m, int item, const Params& p, const int32_t* off,
+                                           int total_full, int64_t chunk, int cap) {
+    m.item = item;
+    const int cg = item / p.hkv;
+    m.h = item - cg * p.hkv;
+    int blo = 0, bhi = p.batch;  // largest b whose offset (in the chunk's group) is <= cg
+    if (cg < total_full) {
+        while (bhi - blo > 1) {
+            const int mid = (blo + bhi) >> 1;
+            if ((off[mid] >> kRemBits) <= cg) blo = mid; else bhi = mid;
+        }
+    } else {
+        const int r = cg - total_full;
+        while (bhi - blo > 1) {
+            const int mid = (blo + bhi) >> 1;
+            if ((off[mid] & ((1 << kRemBits) - 1)) <= r) blo = mid; else bhi = mid;
+        }
+    }
+    m.b = blo;
+    m.ctx = p.context_lens[blo];
+    const SeqChunks sc = seq_chunks(m.ctx, cap, chunk);
+    m.c = cg < total_full ? cg - (off[blo] >> kRemBits) : sc.full;
+    m.nchunks = sc.full + sc.rem;
+    m.slot0 = off[blo];
+    m.t0 = int(m.c * chunk);
+    m.page0 = (m.t0 * kTile) / p.block_size;
+    const int32_t* bt = p.block_tables + int64_t(blo) * p.bt_stride;
+#pragma unroll
+    for (int j = 0; j < kPrefetchPages; ++j) m.blk[j] = bt[min(m.page0 + j, p.bt_stride - 1)];
+}
+
 template <bool BF16, bool ROWS_HI>
 __global__ void __launch_bounds__(kThreads, 1)
     paged_attention_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtensorMap tmk,
                            const __grid_constant__ CUtensorMap tmv) {
     constexpr int RC = ROWS_HI ? 16 : 8;
+    constexpr int NS = num_stages<ROWS_HI>();
     extern __shared__ uint8_t smem_raw[];
-    Smem<RC>& sm = *reinterpret_cast<Smem<RC>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    Smem<RC, NS>& sm =
+        *reinterpret_cast<Smem<RC, NS>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
     if (tid == 0) {
-        for (int s = 0; s < kStages; ++s) {
+        for (int s = 0; s < NS; ++s) {
             mbar_init(&sm.full[s], 1);
             mbar_init(&sm.empty[s], kConsumerWarps);
         }
@@ -148,10 +225,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int seg = (p.batch + kThreads - 1) / kThreads;
     const int lo = min(tid * seg, p.batch), hi = min(lo + seg, p.batch);
     int my_tiles = 0;
-    for (int b = lo; b < hi; ++b) {
-        const int ctx = min(p.context_lens[b], cap);
-        my_tiles += ctx > 0 ? (ctx + kTile - 1) / kTile : 0;
-    }
+    for (int b = lo; b < hi; ++b) my_tiles += seq_chunks(p.context_lens[b], cap, 1).nt;
     int total_tiles = 0;
     block_exclusive_scan(my_tiles, sm.red, &total_tiles);
     int64_t chunk;
@@ -166,81 +240,103 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else {
             chunk = int64_t(1) << 30;
         }
+        // Full-chunk offsets are packed into 31 - kRemBits bits.
+        const int64_t max_full = (int64_t(1) << (31 - kRemBits)) - 1;
+        if (int64_t(total_tiles) / chunk > max_full) chunk = (int64_t(total_tiles) + max_full - 1) / max_full;
     }
-    int my_chunks = 0;
+    int my_full = 0, my_rem = 0;
     for (int b = lo; b < hi; ++b) {
-        const int ctx = min(p.context_lens[b], cap);
-        const int64_t nt = ctx > 0 ? (ctx + kTile - 1) / kTile : 0;
-        my_chunks += int((nt + chunk - 1) / chunk);
+        const SeqChunks sc = seq_chunks(p.context_lens[b], cap, chunk);
+        my_full += sc.full;
+        my_rem += sc.rem;
     }
-    int total_chunks = 0;
-    int off = block_exclusive_scan(my_chunks, sm.red, &total_chunks);
+    int total_full = 0, total_rem = 0;
+    int ofull = block_exclusive_scan(my_full, sm.red, &total_full);
+    int orem = block_exclusive_scan(my_rem, sm.red, &total_rem);
     for (int b = lo; b < hi; ++b) {
-        sm.chunk_off[b] = off;
-        const int ctx = min(p.context_lens[b], cap);
-        const int64_t nt = ctx > 0 ? (ctx + kTile - 1) / kTile : 0;
-        off += int((nt + chunk - 1) / chunk);
+        sm.off[b] = (ofull << kRemBits) | orem;
+        const SeqChunks sc = seq_chunks(p.context_lens[b], cap, chunk);
+        ofull += sc.full;
+        orem += sc.rem;
     }
-    if (tid == 0) sm.chunk_off[p.batch] = total_chunks;
+    if (tid == 0) sm.off[p.batch] = (total_full << kRemBits) | total_rem;
     __syncthreads();
-    const int total_items = total_chunks * p.hkv;
+    const int total_items = (total_full + total_rem) * p.hkv;
 
     if (warp == kConsumerWarps) {
         // ------------------------------------------------------------ producer
         if (lane == 0) {
             const uint64_t pol = l2_policy_evict_first();
+            const uint32_t q_bytes = uint32_t(p.group) * kD * 2;  // one query token's rows of this kv head
             int stage = 0;
             uint32_t phase = 0;
             int64_t fills = 0;
             bool ok = true;
-            int item = atomicAdd(&p.ctrl[0], 1);
-            while (ok && item < total_items) {
-                const int next = atomicAdd(&p.ctrl[0], 1);
-                const int cg = item / p.hkv, h = item - cg * p.hkv;
-                int blo = 0, bhi = p.batch;  // largest b with chunk_off[b] <= cg
-                while (bhi - blo > 1) {
-                    const int mid = (blo + bhi) >> 1;
-                    if (sm.chunk_off[mid] <= cg) blo = mid; else bhi = mid;
-                }
-                const int b = blo;
-                const int c = cg - sm.chunk_off[b];
-                const int nchunks = sm.chunk_off[b + 1] - sm.chunk_off[b];
-                const int ctx = min(p.context_lens[b], cap);
+            ItemMeta cur, nxt;
+            const int first_claim = atomicAdd(&p.ctrl[0], 1);
+            cur.item = total_items;
+            if (first_claim < total_items) fetch_meta(cur, first_claim, p, sm.off, total_full, chunk, cap);
+            int claim = atomicAdd(&p.ctrl[0], 1);
+            while (ok && cur.item < total_items) {
+                const int ctx = min(cur.ctx, cap);
                 const int nt = (ctx + kTile - 1) / kTile;
-                const int t0 = int(c * chunk);
+                const int t0 = cur.t0;
                 const int t1 = int(min(int64_t(nt), t0 + chunk));
-                const int32_t* bt = p.block_tables + int64_t(b) * p.bt_stride;
+                const int32_t* bt = p.block_tables + int64_t(cur.b) * p.bt_stride;
+                int next_claim = claim;
+                nxt.item = total_items;
                 for (int t = t0; t < t1; ++t) {
                     if (!mbar_wait(&sm.empty[stage], phase ^ 1)) {
                         atomicOr(&p.ctrl[2], DEV_ERR_WAIT_EMPTY);
                         ok = false;
                         break;
                     }
+                    const bool first = t == t0;
+                    if (first) {  // start fetching the next item while this one streams
+                        if (claim < total_items) fetch_meta(nxt, claim, p, sm.off, total_full, chunk, cap);
+                        next_claim = atomicAdd(&p.ctrl[0], 1);
+                    }
                     const int pos = t * kTile;
                     const int lb = pos / p.block_size;
-                    const int blk = bt[lb];
+                    int blk;
+                    const int j = lb - cur.page0;
+                    if (j < kPrefetchPages) {
+                        blk = cur.blk[0];
+#pragma unroll
+                        for (int u = 1; u < kPrefetchPages; ++u)
+                            if (j == u) blk = cur.blk[u];
+                    } else {
+                        blk = bt[lb];
+                    }
                     const int y = (blk >= 0 && blk < p.num_blocks) ? blk * p.block_size + (pos - lb * p.block_size)
                                                                    : p.num_blocks * p.block_size;
                     Header& hd = sm.hdr[stage];
-                    hd.item = item;
-                    hd.b = b;
-                    hd.h = h;
+                    hd.item = cur.item;
+                    hd.b = cur.b;
+                    hd.h = cur.h;
                     hd.tile = t;
-                    hd.flags = (t == t0 ? kFirst : 0) | (t == t1 - 1 ? kLast : 0);
+                    hd.flags = (first ? kFirst : 0) | (t == t1 - 1 ? kLast : 0);
                     hd.ctx = ctx;
-                    hd.nchunks = nchunks;
-                    hd.chunk = c;
-                    mbar_arrive_expect_tx(&sm.full[stage], kStageBytes);
+                    hd.nchunks = cur.nchunks;
+                    hd.slot0 = cur.slot0;
+                    mbar_arrive_expect_tx(&sm.full[stage], kStageBytes + (first ? q_bytes * p.lq : 0u));
                     uint8_t* st = sm.stages[stage];
-                    const int x = h * kD;
+                    const int x = cur.h * kD;
                     tma_load_2d(st, &tmk, x, y, &sm.full[stage], pol);
                     tma_load_2d(st + kHalfBytes, &tmk, x + 64, y, &sm.full[stage], pol);
                     tma_load_2d(st + 2 * kHalfBytes, &tmv, x, y, &sm.full[stage], pol);
                     tma_load_2d(st + 3 * kHalfBytes, &tmv, x + 64, y, &sm.full[stage], pol);
+                    if (first) {
+                        const uint16_t* qsrc = p.q + int64_t(cur.b) * p.lq * p.q_stride + int64_t(cur.h) * p.group * kD;
+                        for (int jq = 0; jq < p.lq; ++jq)
+                            bulk_load(sm.qbuf[stage] + jq * q_bytes, qsrc + int64_t(jq) * p.q_stride, q_bytes,
+                                      &sm.full[stage]);
+                    }
                     ++fills;
-                    if (++stage == kStages) { stage = 0; phase ^= 1; }
+                    if (++stage == NS) { stage = 0; phase ^= 1; }
                 }
-                item = next;
+                cur = nxt;
+                claim = next_claim;
             }
             if (ok) {
                 if (mbar_wait(&sm.empty[stage], phase ^ 1)) {
@@ -252,12 +348,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
             if (!ok) {
-                // Error path: wait (bounded) for every TMA fill still in flight
+                // Error path: wait (bounded) for every copy still in flight
                 // before the CTA's shared memory is released.
-                for (int s = 0; s < kStages; ++s) {
+                for (int s = 0; s < NS; ++s) {
                     if (fills <= s) break;
-                    const int64_t last = s + ((fills - 1 - s) / kStages) * kStages;
-                    if (!mbar_wait(&sm.full[s], uint32_t((last / kStages) & 1))) atomicOr(&p.ctrl[2], DEV_ERR_WAIT_DRAIN);
+                    const int64_t last = s + ((fills - 1 - s) / NS) * NS;
+                    if (!mbar_wait(&sm.full[s], uint32_t((last / NS) & 1))) atomicOr(&p.ctrl[2], DEV_ERR_WAIT_DRAIN);
                 }
             }
         }
@@ -288,19 +384,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             const Header hd = sm.hdr[stage];
             if (hd.item < 0) break;
             if (hd.flags & kFirst) {
+                const uint32_t* qs = reinterpret_cast<const uint32_t*>(sm.qbuf[stage]);
 #pragma unroll
                 for (int hr = 0; hr < 2; ++hr) {
                     const int r = g + 8 * hr;
-                    const bool valid = r < p.rows;
-                    const int j = valid ? r / p.group : 0;
-                    const int gq = valid ? r - j * p.group : 0;
-                    lim[hr] = valid ? hd.ctx - p.lq + j : -1;
-                    const uint32_t* qrow = reinterpret_cast<const uint32_t*>(
-                        p.q + (int64_t(hd.b) * p.lq + j) * p.q_stride + int64_t(hd.h * p.group + gq) * kD);
+                    const bool valid = (hr == 0 || ROWS_HI) && r < p.rows;
+                    lim[hr] = valid ? hd.ctx - p.lq + r / p.group : -1;
 #pragma unroll
                     for (int kk = 0; kk < 8; ++kk) {
-                        qa[kk][hr] = valid ? __ldg(qrow + kk * 8 + t4) : 0u;
-                        qa[kk][2 + hr] = valid ? __ldg(qrow + kk * 8 + 4 + t4) : 0u;
+                        qa[kk][hr] = valid ? qs[r * (kD / 2) + kk * 8 + t4] : 0u;
+                        qa[kk][2 + hr] = valid ? qs[r * (kD / 2) + kk * 8 + 4 + t4] : 0u;
                     }
                     m_run[hr] = -INFINITY;
                     l_run[hr] = 0.f;
@@ -325,19 +418,32 @@ __global__ void __launch_bounds__(kThreads, 1)
                     zeroed = true;
                     __syncwarp();
                 }
-                float s[2][4];
+                // S = Q K^T for this warp's 16 tokens; two accumulator sets halve the dependent chain
+                float s[2][4], s2[2][4];
 #pragma unroll
-                for (int n = 0; n < 2; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+                for (int n = 0; n < 2; ++n)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) s[n][e] = s2[n][e] = 0.f;
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk) {
                     const int c16 = 2 * kk + kadd;
                     const uint32_t addr = st + (kk >> 2) * kHalfBytes + tok_k * 128 + (((c16 & 7) ^ rr) << 4);
                     uint32_t b0, b1, b2, b3;
                     ldsm_x4(b0, b1, b2, b3, addr);
-                    mma_16816<BF16>(s[0], qa[kk], b0, b1);
-                    mma_16816<BF16>(s[1], qa[kk], b2, b3);
+                    if (kk < 4) {
+                        mma_16816<BF16>(s[0], qa[kk], b0, b1);
+                        mma_16816<BF16>(s[1], qa[kk], b2, b3);
+                    } else {
+                        mma_16816<BF16>(s2[0], qa[kk], b0, b1);
+                        mma_16816<BF16>(s2[1], qa[kk], b2, b3);
+                    }
                 }
+#pragma unroll
+                for (int n = 0; n < 2; ++n)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) s[n][e] += s2[n][e];
                 float pr[2][4];
+                float alpha[2] = {1.f, 1.f};
 #pragma unroll
                 for (int hr = 0; hr < (ROWS_HI ? 2 : 1); ++hr) {
                     float v[4] = {s[0][2 * hr], s[0][2 * hr + 1], s[1][2 * hr], s[1][2 * hr + 1]};
@@ -351,19 +457,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
                     const float mnew = fmaxf(m_run[hr], mx);
                     const float msl = mnew == -INFINITY ? 0.f : mnew * sl2;
-                    const float alpha = fast_exp2(fmaf(m_run[hr], sl2, -msl));
+                    alpha[hr] = mnew == m_run[hr] ? 1.f : fast_exp2(fmaf(m_run[hr], sl2, -msl));
                     float sum = 0.f;
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
                         pr[hr][e] = fast_exp2(fmaf(v[e], sl2, -msl));
                         sum += pr[hr][e];
                     }
-                    l_run[hr] = fmaf(l_run[hr], alpha, sum);
+                    l_run[hr] = fmaf(l_run[hr], alpha[hr], sum);
                     m_run[hr] = mnew;
+                }
+                // Rescale O only when some row's running max moved (rare after the first tiles).
+                if (__any_sync(0xffffffffu, alpha[0] != 1.f || alpha[1] != 1.f)) {
 #pragma unroll
                     for (int n = 0; n < 16; ++n) {
-                        o[n][2 * hr] *= alpha;
-                        o[n][2 * hr + 1] *= alpha;
+                        o[n][0] *= alpha[0];
+                        o[n][1] *= alpha[0];
+                        if constexpr (ROWS_HI) {
+                            o[n][2] *= alpha[1];
+                            o[n][3] *= alpha[1];
+                        }
                     }
                 }
                 uint32_t pa[4];
@@ -389,39 +502,66 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (zeroed) fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(&sm.empty[stage]);
-            if (++stage == kStages) { stage = 0; phase ^= 1; }
+            if (++stage == NS) { stage = 0; phase ^= 1; }
 
             if (hd.flags & kLast) {
-                // ---- combine the four warps' states of this item ----
+                // ---- combine the eight warps' states of this item ----
 #pragma unroll
                 for (int hr = 0; hr < 2; ++hr) {
                     l_run[hr] += __shfl_xor_sync(0xffffffffu, l_run[hr], 1);
                     l_run[hr] += __shfl_xor_sync(0xffffffffu, l_run[hr], 2);
                 }
+                constexpr int kHalf = kConsumerWarps / 2;
+                // 8 -> 4: warps 4-7 hand their state to warps 0-3, which merge it in registers.
+                if (warp >= kHalf) {
 #pragma unroll
-                for (int hr = 0; hr < (ROWS_HI ? 2 : 1); ++hr) {
-                    const int r = g + 8 * hr;
-                    if (t4 == 0) {
-                        sm.cm[warp][r] = m_run[hr];
-                        sm.cl[warp][r] = l_run[hr];
+                    for (int hr = 0; hr < (ROWS_HI ? 2 : 1); ++hr) {
+                        const int r = g + 8 * hr;
+                        if (t4 == 0) {
+                            sm.cm[warp][r] = m_run[hr];
+                            sm.cl[warp][r] = l_run[hr];
+                        }
+#pragma unroll
+                        for (int n = 0; n < 16; ++n)
+                            *reinterpret_cast<float2*>(&sm.co[warp - kHalf][r][8 * n + 2 * t4]) =
+                                make_float2(o[n][2 * hr], o[n][2 * hr + 1]);
                     }
-#pragma unroll
-                    for (int n = 0; n < 16; ++n)
-                        *reinterpret_cast<float2*>(&sm.co[warp][r][8 * n + 2 * t4]) =
-                            make_float2(o[n][2 * hr], o[n][2 * hr + 1]);
                 }
                 named_bar_sync(kSplitBarrier, kConsumers);
+                if (warp < kHalf) {
+#pragma unroll
+                    for (int hr = 0; hr < (ROWS_HI ? 2 : 1); ++hr) {
+                        const int r = g + 8 * hr;
+                        const float mb = sm.cm[warp + kHalf][r], lb = sm.cl[warp + kHalf][r];
+                        const float M = fmaxf(m_run[hr], mb);
+                        const float sa = M == -INFINITY ? 0.f : fast_exp2((m_run[hr] - M) * sl2);
+                        const float sb = M == -INFINITY ? 0.f : fast_exp2((mb - M) * sl2);
+#pragma unroll
+                        for (int n = 0; n < 16; ++n) {
+                            float2* cp = reinterpret_cast<float2*>(&sm.co[warp][r][8 * n + 2 * t4]);
+                            const float2 ob = *cp;
+                            *cp = make_float2(o[n][2 * hr] * sa + ob.x * sb, o[n][2 * hr + 1] * sa + ob.y * sb);
+                        }
+                        if (t4 == 0) {
+                            sm.cm[warp][r] = M;
+                            sm.cl[warp][r] = l_run[hr] * sa + lb * sb;
+                        }
+                    }
+                }
+                named_bar_sync(kSplitBarrier, kConsumers);
+                // 4 -> 1 over shared memory, one output element per thread and round.
                 const bool single = hd.nchunks == 1;
                 const int nel = p.rows * kD;
+                const int cslot = hd.item / p.hkv;  // this chunk's partial slot (before x Hkv + h)
                 for (int idx = tid; idx < nel; idx += kConsumers) {
                     const int r = idx >> 7, d = idx & (kD - 1);
                     float M = -INFINITY;
 #pragma unroll
-                    for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, sm.cm[w][r]);
+                    for (int w = 0; w < kHalf; ++w) M = fmaxf(M, sm.cm[w][r]);
                     float den = 0.f, acc = 0.f;
                     if (M != -INFINITY) {
 #pragma unroll
-                        for (int w = 0; w < kConsumerWarps; ++w) {
+                        for (int w = 0; w < kHalf; ++w) {
                             const float sc = fast_exp2((sm.cm[w][r] - M) * sl2);
                             den = fmaf(sm.cl[w][r], sc, den);
                             acc = fmaf(sm.co[w][r][d], sc, acc);
@@ -432,31 +572,36 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const int j = r / p.group, gq = r - j * p.group;
                         p.out[((int64_t(hd.b) * p.lq + j) * p.hq + hd.h * p.group + gq) * kD + d] = to_bits16<BF16>(val);
                     } else {
-                        p.part_o[(int64_t(hd.item) * p.rows + r) * kD + d] = val;
-                        if (d == 0)
-                            p.part_lse[int64_t(hd.item) * p.rows + r] = den > 0.f ? fmaf(M, sl2, fast_log2(den)) : -INFINITY;
+                        const int64_t it = int64_t(cslot) * p.hkv + hd.h;
+                        p.part_o[(it * p.rows + r) * kD + d] = val;
+                        if (d == 0) p.part_lse[it * p.rows + r] = den > 0.f ? fmaf(M, sl2, fast_log2(den)) : -INFINITY;
                     }
                 }
                 if (!single) {
-                    __threadfence();
+                    // Publish this chunk (one release fence per CTA, cumulative over
+                    // the barrier), then count it; the last chunk's CTA merges.
                     named_bar_sync(kSplitBarrier, kConsumers);
                     if (tid == 0) {
+                        __threadfence();
                         const int prev = atomicAdd(&p.counters[hd.b * p.hkv + hd.h], 1);
-                        sm.flag = (prev == hd.nchunks - 1);
+                        const bool last = prev == hd.nchunks - 1;
+                        if (last) __threadfence();
+                        sm.flag = last;
                     }
                     named_bar_sync(kSplitBarrier, kConsumers);
                     if (sm.flag) {
-                        __threadfence();
-                        const int64_t item0 = int64_t(sm.chunk_off[hd.b]) * p.hkv + hd.h;
+                        const int full = hd.nchunks - (seq_chunks(hd.ctx, cap, chunk).rem);
                         for (int idx = tid; idx < nel; idx += kConsumers) {
                             const int r = idx >> 7, d = idx & (kD - 1);
                             float L = -INFINITY;
-                            for (int c = 0; c < hd.nchunks; ++c)
-                                L = fmaxf(L, __ldcg(p.part_lse + (item0 + int64_t(c) * p.hkv) * p.rows + r));
+                            for (int c = 0; c < hd.nchunks; ++c) {
+                                const int64_t it = int64_t(chunk_slot(hd.slot0, c, full, total_full)) * p.hkv + hd.h;
+                                L = fmaxf(L, __ldcg(p.part_lse + it * p.rows + r));
+                            }
                             float den = 0.f, acc = 0.f;
                             if (L != -INFINITY) {
                                 for (int c = 0; c < hd.nchunks; ++c) {
-                                    const int64_t it = item0 + int64_t(c) * p.hkv;
+                                    const int64_t it = int64_t(chunk_slot(hd.slot0, c, full, total_full)) * p.hkv + hd.h;
                                     const float w = fast_exp2(__ldcg(p.part_lse + it * p.rows + r) - L);
                                     den += w;
                                     acc = fmaf(w, __ldcg(p.part_o + (it * p.rows + r) * kD + d), acc);
@@ -530,8 +675,9 @@ extern "C" int32_t b200_paged_attention(void* out, const void* q, int64_t q_stri
                  "paged_attention: block_table_stride %d out of range", block_table_stride);
     B200_REQUIRE(q_stride_token >= int64_t(num_heads) * head_dim && q_stride_token % 2 == 0,
                  "paged_attention: q token stride %lld", (long long)q_stride_token);
-    B200_REQUIRE((reinterpret_cast<uintptr_t>(q) & 3) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0,
-                 "paged_attention: q must be 4-byte and out 16-byte aligned");
+    B200_REQUIRE((reinterpret_cast<uintptr_t>(q) & 15) == 0 && q_stride_token % 8 == 0 &&
+                     (reinterpret_cast<uintptr_t>(out) & 15) == 0,
+                 "paged_attention: q and out must be 16-byte aligned, q token stride a multiple of 8");
     if (int64_t(batch) * num_kv_heads > kCounterSlots)
         return fail(B200_ERR_UNSUPPORTED, "paged_attention: batch * num_kv_heads > %d", kCounterSlots);
     if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255) || workspace_bytes < kFixedBytes)
@@ -586,7 +732,7 @@ extern "C" int32_t b200_paged_attention(void* out, const void* q, int64_t q_stri
     } else {
         fn = hi ? (const void*)paged_attention_kernel<false, true> : (const void*)paged_attention_kernel<false, false>;
     }
-    smem = hi ? smem_bytes<16>() : smem_bytes<8>();
+    smem = hi ? smem_bytes<true>() : smem_bytes<false>();
     ensure_smem_attr(fn, smem);
     if (bf16) {
         if (hi) paged_attention_kernel<true, true><<<grid, block, smem, s>>>(prm, tmk, tmv);
@@ -688,8 +834,9 @@ extern "C" int32_t b200_paged_attention_noalloc(void* out, const void* q, int64_
                  "paged_attention_noalloc: block_table_stride %d out of range", block_table_stride);
     B200_REQUIRE(q_stride_token >= int64_t(num_heads) * head_dim && q_stride_token % 2 == 0,
                  "paged_attention_noalloc: q token stride %lld", (long long)q_stride_token);
-    B200_REQUIRE((reinterpret_cast<uintptr_t>(q) & 3) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0,
-                 "paged_attention_noalloc: q must be 4-byte and out 16-byte aligned");
+    B200_REQUIRE((reinterpret_cast<uintptr_t>(q) & 15) == 0 && q_stride_token % 8 == 0 &&
+                     (reinterpret_cast<uintptr_t>(out) & 15) == 0,
+                 "paged_attention_noalloc: q and out must be 16-byte aligned, q token stride a multiple of 8");
     const int64_t pairs = int64_t(batch) * num_kv_heads;
     const int64_t max_items = int64_t(kNoAllocScratchBytes - kNoAllocFixedBytes) / (int64_t(rows) * (kD + 1) * 4);
     if (pairs > kNoAllocCounterSlots || pairs > max_items)
@@ -745,7 +892,7 @@ extern "C" int32_t b200_paged_attention_noalloc(void* out, const void* q, int64_
         fn = hi ? (const void*)paged_attention_kernel<true, true> : (const void*)paged_attention_kernel<true, false>;
     else
         fn = hi ? (const void*)paged_attention_kernel<false, true> : (const void*)paged_attention_kernel<false, false>;
-    const int smem = hi ? smem_bytes<16>() : smem_bytes<8>();
+    const int smem = hi ? smem_bytes<true>() : smem_bytes<false>();
     ensure_smem_attr(fn, smem);
     if (bf16) {
         if (hi) paged_attention_kernel<true, true><<<grid, block, smem, s>>>(prm, tmk, tmv);

@@ -60,7 +60,7 @@ def test_noalloc_matches_workspace_entry_point(pkg, ctx, hq, hkv, lq, seed):
 def test_noalloc_rejects_batches_beyond_its_scratch(pkg):
     lib = pkg.lib()
     dummy = ctypes.c_void_p(256)
-    rc = lib.b200_paged_attention_noalloc(dummy, dummy, 4096, dummy, dummy, 8, 256, dummy, 4, dummy, 4096, 1, 32, 8,
+    rc = lib.b200_paged_attention_noalloc(dummy, dummy, 4096, dummy, dummy, 8, 256, dummy, 4, dummy, 2048, 1, 32, 8,
                                           128, 0.088, 1, None)
     assert rc == B200_ERR_WORKSPACE
     assert b"exceeds the built-in" in lib.b200_last_error()
