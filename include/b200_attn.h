@@ -146,7 +146,9 @@ B200_API int32_t b200_workspace_error(const void* workspace, void* stream, int32
  *                            max_seqlen_q=..., max_seqlen_k=...,
  *                            softmax_scale=scale, causal=True,
  *                            block_table=block_tables)
- * q/out : [total_q, Hq, D] (out contiguous)
+ * q/out : [total_q, Hq, D] (out contiguous, 16-byte aligned); total_q and
+ *         total_k_rows are the row counts of the q and k/v buffers (the TMA
+ *         descriptors never reach past them)
  * Without a block table k/v are packed token rows [total_k, Hkv, D] and the
  * keys of sequence s are rows cu_seqlens_k[s] .. cu_seqlens_k[s+1]-1.
  * With a block table k/v are the layer's caches [num_blocks, block_size,
@@ -159,12 +161,20 @@ B200_API int32_t b200_varlen_prefill(void* out, const void* q, int64_t q_stride_
                             const void* k, int64_t k_stride_token,
                             const void* v, int64_t v_stride_token,
                             const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k,
-                            int32_t num_seqs, int32_t max_seqlen_q, int32_t max_seqlen_k,
+                            int32_t num_seqs, int32_t total_q,
+                            int32_t max_seqlen_q, int32_t max_seqlen_k,
                             int32_t total_k_rows,
                             const int32_t* block_tables, int32_t block_table_stride,
                             int32_t block_size,
                             int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
                             float softmax_scale, int32_t dtype, void* stream);
+
+/*
+ * Copies the prefill kernels' device-side error word to *flag after
+ * synchronising `stream`; non-zero means a bounded wait inside the kernel gave
+ * up (results of that call undefined).  For tests and diagnostics only.
+ */
+B200_API int32_t b200_varlen_prefill_error(void* stream, int32_t* flag);
 
 /*
  * Speculative-decoding acceptance sampling (standard rejection scheme):

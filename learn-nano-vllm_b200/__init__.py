@@ -13,7 +13,7 @@ Public API
   install                   patch nano-vLLM to use this package's Attention
   context                   mirror of nanovllm.utils.context
 """
-from . import context
+from . import context, ops
 from ._native import B200Error, lib
 from .attention import Attention
 from .integrate import install

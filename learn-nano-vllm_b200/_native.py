@@ -24,8 +24,9 @@ SIGNATURES = {
     "b200_paged_attention_noalloc": (_I32, [_P, _P, _I64, _P, _P, _I32, _I32, _P, _I32, _P, _I32, _I32, _I32,
                                             _I32, _I32, _F, _I32, _P]),
     "b200_workspace_error": (_I32, [_P, _P, ctypes.POINTER(ctypes.c_int32)]),
-    "b200_varlen_prefill": (_I32, [_P, _P, _I64, _P, _I64, _P, _I64, _P, _P, _I32, _I32, _I32, _I32, _P, _I32,
-                                   _I32, _I32, _I32, _I32, _F, _I32, _P]),
+    "b200_varlen_prefill": (_I32, [_P, _P, _I64, _P, _I64, _P, _I64, _P, _P, _I32, _I32, _I32, _I32, _I32, _P,
+                                   _I32, _I32, _I32, _I32, _I32, _F, _I32, _P]),
+    "b200_varlen_prefill_error": (_I32, [_P, ctypes.POINTER(ctypes.c_int32)]),
     "b200_spec_accept_workspace_size": (_SZ, [_I32, _I32, _I32]),
     "b200_spec_accept": (_I32, [_P, _P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _P, _SZ, _P]),
 }

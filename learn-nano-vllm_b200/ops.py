@@ -23,6 +23,11 @@ def _stream(t: torch.Tensor) -> int:
     return torch.cuda.current_stream(t.device).cuda_stream
 
 
+def _row_stride(t: torch.Tensor) -> int:
+    """Row stride of a 2-D table; a single-row table may carry any stride on its size-1 dim."""
+    return t.stride(0) if t.size(0) > 1 else max(t.size(1), 1)
+
+
 def _require_cuda(*ts):
     dev = ts[0].device
     for t in ts:
@@ -114,7 +119,7 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
     if workspace is None:
         workspace = paged_workspace(q.device, Lq, Hq // Hkv, B * Hkv)
     rc = lib().b200_paged_attention(out.data_ptr(), q.data_ptr(), q_tok, k_cache.data_ptr(), v_cache.data_ptr(), NB, bs, block_tables.data_ptr(),
-                                    block_tables.stride(0), context_lens.data_ptr(), B, Lq, Hq, Hkv, D,
+                                    _row_stride(block_tables), context_lens.data_ptr(), B, Lq, Hq, Hkv, D,
                                     float(softmax_scale), _DTYPES[q.dtype], workspace.data_ptr(),
                                     workspace.numel(), _stream(q))
     check(rc, "paged_attention")
@@ -133,6 +138,14 @@ def flash_attn_with_kvcache(q, k_cache, v_cache, cache_seqlens=None, block_table
         raise NotImplementedError("non-causal multi-query paged attention")
     scale = q.size(-1) ** -0.5 if softmax_scale is None else softmax_scale
     return paged_attention(q, k_cache, v_cache, cache_seqlens, block_table, scale, out=out)
+
+
+def prefill_error() -> int:
+    """Device error word of the prefill kernels (synchronises the current stream)."""
+    flag = ctypes.c_int32(0)
+    check(lib().b200_varlen_prefill_error(torch.cuda.current_stream().cuda_stream, ctypes.byref(flag)),
+          "varlen_prefill_error")
+    return flag.value
 
 
 def workspace_error(workspace: torch.Tensor) -> int:
@@ -166,7 +179,7 @@ def flash_attn_varlen_func(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, ma
         assert block_table.dtype == torch.int32 and block_table.stride(1) == 1
         k_stride = v_stride = Hkv * D
         total_k_rows = NB * bs
-        bt_ptr, bt_stride = block_table.data_ptr(), block_table.stride(0)
+        bt_ptr, bt_stride = block_table.data_ptr(), _row_stride(block_table)
     else:
         Tk, Hkv, Dk = k.shape
         assert k.stride(-1) == 1 and k.stride(-2) == D and v.stride(-1) == 1 and v.stride(-2) == D
@@ -180,7 +193,7 @@ def flash_attn_varlen_func(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, ma
     if Tq == 0 or S == 0:
         return out
     rc = lib().b200_varlen_prefill(out.data_ptr(), q.data_ptr(), q.stride(0), k.data_ptr(), k_stride, v.data_ptr(),
-                                   v_stride, cu_seqlens_q.data_ptr(), cu_seqlens_k.data_ptr(), S,
+                                   v_stride, cu_seqlens_q.data_ptr(), cu_seqlens_k.data_ptr(), S, Tq,
                                    int(max_seqlen_q), int(max_seqlen_k), total_k_rows, bt_ptr, bt_stride, bs,
                                    Hq, Hkv, D, float(scale), _DTYPES[q.dtype], _stream(q))
     check(rc, "varlen_prefill")
