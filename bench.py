@@ -53,15 +53,19 @@ def parse():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--workload", choices=["decode", "prefill", "verify"], default="decode",
+                    help="decode = config 5 (the bench line); prefill = config 3; verify = config 4 (1 GPU)")
     ap.add_argument("--batch", type=int, default=BATCH,
                     help="sequences in the batch (profiling runs use a smaller batch; the bench line uses 512)")
     return ap.parse_args()
 
 
 def workload(batch=BATCH):
-    from oracle.cases import config5_context_lens
-    ctx = config5_context_lens(batch, SIGMA, seed=0, cap=CAP)
-    return ctx
+    """Config 5 context lengths: lognormal(ln 2048, SIGMA) capped at CAP, seed 0
+    (the same draw as the tests' case factory)."""
+    rng = np.random.default_rng(0)
+    c = np.exp(rng.normal(np.log(2048.0), SIGMA, size=batch))
+    return np.clip(np.rint(c), 1, CAP).astype(np.int32)
 
 
 def step_bytes(ctx, hq, hkv, width):
@@ -250,6 +254,153 @@ def config_dict(world, ctx):
             "l2": "no flush: per-step KV bytes per rank >> 126 MB L2"}
 
 
+def _time(torch, stream, fn, steps, warmup):
+    for _ in range(max(warmup, 3)):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def run_prefill(args, pkg, torch, dev):
+    """Config 3: 64 sequences share a 768-token prefix (3 cached blocks), unique
+    suffixes U[64, 512]; Qwen3-0.6B attention shape (16 q / 8 kv heads); scatter
+    of the suffix K/V + causal prefill over the paged cache."""
+    hq, hkv, d, bs, prefix = 16, 8, 128, 256, 768
+    rng = np.random.default_rng(0)
+    suffix = rng.integers(64, 513, size=64).astype(np.int32)
+    lk = suffix + prefix
+    nblk = (lk + bs - 1) // bs
+    pool = 3 + int((nblk - 3).sum())
+    perm = rng.permutation(pool).astype(np.int32)
+    bt = np.full((64, int(nblk.max())), -1, np.int32)
+    o = 3
+    for s_ in range(64):
+        bt[s_, :3] = perm[:3]
+        bt[s_, 3:nblk[s_]] = perm[o:o + nblk[s_] - 3]
+        o += nblk[s_] - 3
+    slots = np.concatenate([bt[s_, np.arange(prefix, lk[s_]) // bs] * bs + np.arange(prefix, lk[s_]) % bs
+                            for s_ in range(64)]).astype(np.int32)
+    T = int(suffix.sum())
+    g = torch.Generator(device=dev).manual_seed(3)
+    rnd = lambda *shape: (torch.randn(*shape, generator=g, device=dev) * d ** -0.5).to(torch.bfloat16)
+    kc, vc = rnd(pool, bs, hkv, d), rnd(pool, bs, hkv, d)
+    q, kn, vn = rnd(T, hq, d), rnd(T, hkv, d), rnd(T, hkv, d)
+    cu_q = torch.from_numpy(np.concatenate([[0], np.cumsum(suffix)]).astype(np.int32)).to(dev)
+    cu_k = torch.from_numpy(np.concatenate([[0], np.cumsum(lk)]).astype(np.int32)).to(dev)
+    btd, sl = torch.from_numpy(bt).to(dev), torch.from_numpy(slots).to(dev)
+    out = torch.empty_like(q)
+
+    def attn():
+        pkg.flash_attn_varlen_func(q, kc, vc, cu_seqlens_q=cu_q, cu_seqlens_k=cu_k, max_seqlen_q=int(suffix.max()),
+                                   max_seqlen_k=int(lk.max()), softmax_scale=d ** -0.5, causal=True,
+                                   block_table=btd, out=out)
+
+    def step():
+        pkg.store_kvcache(kn, vn, kc, vc, sl)
+        attn()
+
+    stream = torch.cuda.current_stream(dev)
+    flops = 4.0 * hq * d * float((suffix.astype(np.float64) * prefix + suffix * (suffix + 1) / 2.0).sum())
+    with ClockSampler(dev.index or 0) as clk:
+        ms = _time(torch, stream, step, args.steps, args.warmup)
+        kms = _time(torch, stream, attn, args.steps, args.warmup)
+    assert pkg.ops.prefill_error() == 0
+    peak = _peak_tflops()
+    print(json.dumps({
+        "metric": "prefix-cached prefill attn TFLOP/s (useful causal flops)", "value": round(flops / (ms / 1e3) / 1e12, 2),
+        "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "dtype": "bf16", "data": "synthetic (seeded random bf16)",
+        "config": {"workload": "config3: 64 seqs, shared 768-token prefix, suffix U[64,512], 16/8 heads, D 128",
+                   "tokens": T},
+        "roofline": {"bound": "tensor", "kernel": "prefill_kernel", "achieved": round(flops / (kms / 1e3) / 1e12, 1),
+                     "peak": peak[0], "peak_kind": peak[1], "unit": "TFLOP/s",
+                     "frac": round(flops / (kms / 1e3) / 1e12 / peak[0], 4), "us_per_launch": round(kms * 1e3, 2),
+                     "flops_per_launch": flops},
+        "clocks": clk.summary()}), flush=True)
+
+
+def run_verify(args, pkg, torch, dev):
+    """Config 4: speculative verify on the Qwen3-0.6B attention shape -- B=128,
+    k=4 drafts (5 queries each), context U[512, 4096]; scatter of the 5 new
+    tokens, (k+1)-query paged attention, then acceptance sampling over
+    vocab 151936 (logits N(0, 2^2), drafts correlated with the target)."""
+    B, k, V, hq, hkv, d, bs = 128, 4, 151936, 16, 8, 128, 256
+    rng = np.random.default_rng(0)
+    ctx = rng.integers(512, 4097, size=B).astype(np.int32)
+    nblk = (ctx + bs - 1) // bs
+    nb = int(nblk.sum())
+    perm = rng.permutation(nb).astype(np.int32)
+    bt = np.full((B, int(nblk.max())), -1, np.int32)
+    off = np.concatenate([[0], np.cumsum(nblk)])
+    for b in range(B):
+        bt[b, :nblk[b]] = perm[off[b]:off[b + 1]]
+    pos = np.concatenate([np.arange(c - k - 1, c) for c in ctx])
+    rows = np.repeat(np.arange(B), k + 1)
+    slots = (bt[rows, pos // bs] * bs + pos % bs).astype(np.int32)
+    g = torch.Generator(device=dev).manual_seed(4)
+    rnd = lambda *shape: (torch.randn(*shape, generator=g, device=dev) * d ** -0.5).to(torch.bfloat16)
+    kc, vc = rnd(nb, bs, hkv, d), rnd(nb, bs, hkv, d)
+    q, kn, vn = rnd(B, k + 1, hq, d), rnd(B * (k + 1), hkv, d), rnd(B * (k + 1), hkv, d)
+    cl, btd, sl = (torch.from_numpy(x).to(dev) for x in (ctx, bt, slots))
+    tl = torch.randn(B, k + 1, V, generator=g, device=dev) * 2.0
+    dl = (tl[:, :k] + torch.randn(B, k, V, generator=g, device=dev)).contiguous()
+    gum = -torch.log(-torch.log(torch.rand(B, k, V, generator=g, device=dev).clamp_min(1e-20)))
+    dt = (dl + gum).argmax(-1).to(torch.int32)
+    del gum
+    ua, us = torch.rand(B, k, generator=g, device=dev), torch.rand(B, generator=g, device=dev)
+    out = torch.empty_like(q)
+    ws = pkg.paged_workspace(dev, k + 1, hq // hkv, B * hkv)
+    sws = torch.empty(max(pkg.lib().b200_spec_accept_workspace_size(B, k, V), 256), dtype=torch.uint8, device=dev)
+
+    def attn():
+        pkg.paged_attention(q, kc, vc, cl, btd, d ** -0.5, out=out, workspace=ws)
+
+    def accept():
+        pkg.spec_accept(tl, dl, dt, ua, us, workspace=sws)
+
+    def step():
+        pkg.store_kvcache(kn, vn, kc, vc, sl)
+        attn()
+        accept()
+
+    stream = torch.cuda.current_stream(dev)
+    attn_bytes = int(ctx.sum()) * 2 * hkv * d * 2 + B * (k + 1) * hq * d * 2 * 2
+    acc_bytes = (2 * k + 1) * B * V * 4
+    with ClockSampler(dev.index or 0) as clk:
+        ms = _time(torch, stream, step, args.steps, args.warmup)
+        ams = _time(torch, stream, attn, args.steps, args.warmup)
+        sms = _time(torch, stream, accept, args.steps, args.warmup)
+    flops = 4.0 * float(ctx.sum()) * (k + 1) * hq * d
+    hbm = measured_peak()
+    toks, num = pkg.spec_accept(tl, dl, dt, ua, us, workspace=sws)
+    print(json.dumps({
+        "metric": "speculative verify step ms (attention + acceptance)", "value": round(ms, 4), "unit": "ms",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": False, "dtype": "bf16/fp32",
+        "data": "synthetic (seeded)", "config": {"workload": "config4: B=128, k=4, ctx U[512,4096], 16/8 heads, V 151936"},
+        "attention": {"us": round(ams * 1e3, 2), "GBps": round(attn_bytes / (ams / 1e3) / 1e9, 1),
+                      "frac_hbm": round(attn_bytes / (ams / 1e3) / 1e9 / hbm[0], 4),
+                      "TFLOPs": round(flops / (ams / 1e3) / 1e12, 2)},
+        "acceptance": {"us": round(sms * 1e3, 2), "GBps": round(acc_bytes / (sms / 1e3) / 1e9, 1),
+                       "frac_hbm": round(acc_bytes / (sms / 1e3) / 1e9 / hbm[0], 4),
+                       "mean_accepted": round(float(num.float().mean().item()) - 1, 3)},
+        "clocks": clk.summary()}), flush=True)
+
+
+def _peak_tflops():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured (burst)"
+    except Exception:
+        return 1590.0, "fallback"
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -268,6 +419,10 @@ def main():
     pkg = __graft_entry__.load_package()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    if args.workload != "decode":
+        assert world == 1, "the prefill / verify workloads run on one GPU"
+        (run_prefill if args.workload == "prefill" else run_verify)(args, pkg, torch, dev)
+        return
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)

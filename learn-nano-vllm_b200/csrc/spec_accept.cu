@@ -11,10 +11,13 @@
 //              k*1024 + 4i + c (k outer, c inner), a warp xor-butterfly
 //              (16,8,4,2,1) combines 32 threads, 8 warp sums and then the
 //              tile sums are added left to right;
+//   normaliser: per tile M_t = tile max, S_t = tile sum of exp_c(x - M_t);
+//              M = max_t M_t, S = sum_t S_t * exp_c(M_t - M) (left to right);
+//              p_j = exp_c(x_j - M) / S; non-finite logits weigh 0;
 //   sampling: inverse CDF over tile sums, thread sums of the chosen tile,
 //              then the thread's 16 elements, each scanned left to right.
 //
-// Kernel 1 (one CTA per logits row): max and canonical sum of exp per row.
+// Kernel 1 (one CTA per logits row, one pass over the row): M and S.
 // Kernel 2 (one CTA per sequence): decisions from the per-row statistics,
 // then one pass over the rejected row (residual) or the bonus row.
 #include "common.cuh"
@@ -61,57 +64,80 @@ __device__ __forceinline__ const float* row_ptr(const Rows& R, int r, int* b_out
 
 __device__ __forceinline__ float scaled(float l, float T) { return T > 0.f ? __fdiv_rn(l, T) : l; }
 
-// Canonical thread partial of tile t for thread i: elements k*1024 + 4i + c.
-template <typename F>
-__device__ __forceinline__ float thread_partial(int t, int i, int V, F&& w) {
-    float acc = 0.f;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            const int j = t * kTileElems + k * 1024 + 4 * i + c;
-            if (j < V) acc = __fadd_rn(acc, w(j));
-        }
-    }
-    return acc;
-}
-
 __device__ __forceinline__ float warp_butterfly(float v) {
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
     return v;
 }
 
+// One tile (4096 values) of a row as this thread's 16 values, in the fixed
+// order k = 0..3 (stride 1024), c = 0..3; values past V read as -inf.
+__device__ __forceinline__ void load_tile(const float* x, int V, int t, float T, bool vec, float (&v)[16]) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int base = t * kTileElems + k * 1024 + 4 * int(threadIdx.x);
+        if (vec && base + 3 < V) {
+            const float4 f = __ldg(reinterpret_cast<const float4*>(x + base));
+            v[4 * k] = scaled(f.x, T);
+            v[4 * k + 1] = scaled(f.y, T);
+            v[4 * k + 2] = scaled(f.z, T);
+            v[4 * k + 3] = scaled(f.w, T);
+        } else {
+#pragma unroll
+            for (int c = 0; c < 4; ++c) v[4 * k + c] = base + c < V ? scaled(__ldg(x + base + c), T) : -INFINITY;
+        }
+    }
+}
+
+// Per row: M_t and S_t = fixed-order tile sum of exp_c(x - M_t) for every
+// tile, then M = max M_t and S = sum_t S_t * exp_c(M_t - M).  Each row is read
+// once; the next tile's loads are issued before the current tile's reductions.
 __global__ void __launch_bounds__(kThreads) row_stats_kernel(Rows R, float2* stats) {
-    __shared__ float red[kThreads / 32];
-    __shared__ float wsum[kMaxTiles][kThreads / 32];
+    __shared__ float wred[kThreads / 32];
+    __shared__ float tile_m[kMaxTiles], tile_s[kMaxTiles];
     int b;
     const float* x = row_ptr(R, blockIdx.x, &b);
     const float T = R.temps ? R.temps[b] : 0.f;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    float m = -INFINITY;
-    for (int j = tid; j < R.V; j += kThreads) m = fmaxf(m, scaled(__ldg(x + j), T));
-#pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if (lane == 0) red[warp] = m;
-    __syncthreads();
-    float M = red[0];
-#pragma unroll
-    for (int w = 1; w < kThreads / 32; ++w) M = fmaxf(M, red[w]);
+    const bool vec = (R.V & 3) == 0;
     const int nt = (R.V + kTileElems - 1) / kTileElems;
+    float cur[16], nxt[16];
+    load_tile(x, R.V, 0, T, vec, cur);
     for (int t = 0; t < nt; ++t) {
-        const float part = thread_partial(t, tid, R.V, [&](int j) { return exp_c(__fsub_rn(scaled(__ldg(x + j), T), M)); });
-        const float ws = warp_butterfly(part);
-        if (lane == 0) wsum[t][warp] = ws;
-    }
-    __syncthreads();
-    if (tid == 0) {
-        float S = 0.f;
-        for (int t = 0; t < nt; ++t) {
+        if (t + 1 < nt) load_tile(x, R.V, t + 1, T, vec, nxt);
+        float m = -INFINITY;
+#pragma unroll
+        for (int e = 0; e < 16; ++e) m = fmaxf(m, cur[e]);
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (lane == 0) wred[warp] = m;
+        __syncthreads();
+        float Mt = wred[0];
+#pragma unroll
+        for (int w = 1; w < kThreads / 32; ++w) Mt = fmaxf(Mt, wred[w]);
+        __syncthreads();
+        float acc = 0.f;
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+            if (isfinite(cur[e])) acc = __fadd_rn(acc, exp_c(__fsub_rn(cur[e], Mt)));
+        const float ws = warp_butterfly(acc);
+        if (lane == 0) wred[warp] = ws;
+        __syncthreads();
+        if (tid == 0) {
             float st = 0.f;
-            for (int w = 0; w < kThreads / 32; ++w) st = __fadd_rn(st, wsum[t][w]);
-            S = __fadd_rn(S, st);
+            for (int w = 0; w < kThreads / 32; ++w) st = __fadd_rn(st, wred[w]);
+            tile_m[t] = Mt;
+            tile_s[t] = st;
         }
+        __syncthreads();
+#pragma unroll
+        for (int e = 0; e < 16; ++e) cur[e] = nxt[e];
+    }
+    if (tid == 0) {
+        float M = -INFINITY;
+        for (int t = 0; t < nt; ++t) M = fmaxf(M, tile_m[t]);
+        float S = 0.f;
+        for (int t = 0; t < nt; ++t) S = __fadd_rn(S, __fmul_rn(tile_s[t], exp_c(__fsub_rn(tile_m[t], M))));
         stats[blockIdx.x] = make_float2(M, S);
     }
 }
@@ -159,20 +185,57 @@ struct Weight {
     const float *xt, *xd;
     float T, Mt, St, Md, Sd;
     bool residual;
-    __device__ __forceinline__ float operator()(int j) const {
-        const float p = __fdiv_rn(exp_c(__fsub_rn(scaled(__ldg(xt + j), T), Mt)), St);
+    bool vec;
+    __device__ __forceinline__ float from(float lt, float ld) const {
+        const float p = __fdiv_rn(exp_c(__fsub_rn(scaled(lt, T), Mt)), St);
         if (!residual) return p;
-        const float q = __fdiv_rn(exp_c(__fsub_rn(scaled(__ldg(xd + j), T), Md)), Sd);
+        const float q = __fdiv_rn(exp_c(__fsub_rn(scaled(ld, T), Md)), Sd);
         return fmaxf(__fsub_rn(p, q), 0.f);
     }
+    __device__ __forceinline__ float operator()(int j) const {
+        return from(__ldg(xt + j), residual ? __ldg(xd + j) : 0.f);
+    }
 };
+
+// Fixed-order thread partial of tile t with float4 loads of both rows.
+__device__ __forceinline__ float weight_partial(const Weight& w, int t, int V) {
+    float lt[16], ld[16];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int base = t * kTileElems + k * 1024 + 4 * int(threadIdx.x);
+        if (w.vec && base + 3 < V) {
+            const float4 a = __ldg(reinterpret_cast<const float4*>(w.xt + base));
+            lt[4 * k] = a.x, lt[4 * k + 1] = a.y, lt[4 * k + 2] = a.z, lt[4 * k + 3] = a.w;
+            if (w.residual) {
+                const float4 c = __ldg(reinterpret_cast<const float4*>(w.xd + base));
+                ld[4 * k] = c.x, ld[4 * k + 1] = c.y, ld[4 * k + 2] = c.z, ld[4 * k + 3] = c.w;
+            } else {
+                ld[4 * k] = ld[4 * k + 1] = ld[4 * k + 2] = ld[4 * k + 3] = 0.f;
+            }
+        } else {
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const bool in = base + c < V;
+                lt[4 * k + c] = in ? __ldg(w.xt + base + c) : 0.f;
+                ld[4 * k + c] = in && w.residual ? __ldg(w.xd + base + c) : 0.f;
+            }
+        }
+    }
+    float acc = 0.f;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+        const int j = t * kTileElems + (e >> 2) * 1024 + 4 * int(threadIdx.x) + (e & 3);
+        if (j < V) acc = __fadd_rn(acc, w.from(lt[e], ld[e]));
+    }
+    return acc;
+}
 
 // Canonical inverse-CDF pick over the whole row; -1 if the row has no mass.
 __device__ int canon_pick(const Weight& w, int V, float u, float* part, float* wsum) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int nt = (V + kTileElems - 1) / kTileElems;
     for (int t = 0; t < nt; ++t) {
-        const float pt = thread_partial(t, tid, V, w);
+        const float pt = weight_partial(w, t, V);
         part[t * kThreads + tid] = pt;
         const float ws = warp_butterfly(pt);
         if (lane == 0) wsum[t * (kThreads / 32) + warp] = ws;
@@ -225,26 +288,32 @@ __global__ void __launch_bounds__(kThreads) decide_kernel(Decide d) {
     __shared__ int rej_s;
     const float T = R.temps ? R.temps[b] : 0.f;
     const int rows_t = R.B * (k + 1);
-    if (threadIdx.x == 0) {
-        int rej = k;
-        for (int i = 0; i < k; ++i) {
-            const int x = d.draft[b * k + i];
-            if (x < 0 || x >= V) {
-                rej = i;
-                break;
-            }
+    // Draft position i's decision on lane i (at most 32 drafts), then the
+    // first rejection in order.
+    __shared__ int accept_s[32];
+    if (threadIdx.x < k) {
+        const int i = threadIdx.x;
+        const int x = d.draft[b * k + i];
+        bool acc = false;
+        if (x >= 0 && x < V) {
             const float2 st = d.stats[b * (k + 1) + i];
             const float2 sd = d.stats[rows_t + b * k + i];
             const float* xt = R.tl + (int64_t(b) * (k + 1) + i) * V;
             const float* xd = R.dl + (int64_t(b) * k + i) * V;
             const float p = __fdiv_rn(exp_c(__fsub_rn(scaled(xt[x], T), st.x)), st.y);
             const float q = __fdiv_rn(exp_c(__fsub_rn(scaled(xd[x], T), sd.x)), sd.y);
-            const bool acc = q > 0.f ? (d.ua[b * k + i] < fminf(1.f, __fdiv_rn(p, q))) : (p > 0.f);
-            if (!acc) {
+            acc = q > 0.f ? (d.ua[b * k + i] < fminf(1.f, __fdiv_rn(p, q))) : (p > 0.f);
+        }
+        accept_s[i] = acc;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int rej = k;
+        for (int i = 0; i < k; ++i)
+            if (!accept_s[i]) {
                 rej = i;
                 break;
             }
-        }
         rej_s = rej;
     }
     __syncthreads();
@@ -256,6 +325,7 @@ __global__ void __launch_bounds__(kThreads) decide_kernel(Decide d) {
     w.Mt = st.x;
     w.St = st.y;
     w.residual = rej < k;
+    w.vec = (V & 3) == 0;
     if (rej < k) {
         w.xd = R.dl + (int64_t(b) * k + rej) * V;
         const float2 sd = d.stats[rows_t + b * k + rej];
@@ -304,6 +374,10 @@ extern "C" int32_t b200_spec_accept(int32_t* out_tokens, int32_t* out_num_tokens
     B200_REQUIRE(vocab_size > 0, "spec_accept: vocab_size %d", vocab_size);
     if (vocab_size > kMaxTiles * kTileElems)
         return fail(B200_ERR_UNSUPPORTED, "spec_accept: vocab_size %d > %d", vocab_size, kMaxTiles * kTileElems);
+    if (num_draft > 32) return fail(B200_ERR_UNSUPPORTED, "spec_accept: num_draft %d > 32", num_draft);
+    B200_REQUIRE((reinterpret_cast<uintptr_t>(target_logits) & 15) == 0 &&
+                     (num_draft == 0 || (reinterpret_cast<uintptr_t>(draft_logits) & 15) == 0),
+                 "spec_accept: logits must be 16-byte aligned");
     const size_t need = b200_spec_accept_workspace_size(batch, num_draft, vocab_size);
     if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 15))
         return fail(B200_ERR_WORKSPACE, "spec_accept: workspace needs %zu bytes (16-byte aligned)", need);

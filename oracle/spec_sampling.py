@@ -22,6 +22,10 @@ tokens bit for bit given identical uniforms:
     c = 0..3 inner) left to right; the 32 thread sums of each warp are
     combined by an xor butterfly (16, 8, 4, 2, 1); the 8 warp sums are
     added left to right; tile sums are added left to right;
+  * softmax normaliser of a row: per tile t, M_t = max of the tile and
+    S_t = the tile sum of exp_c(x - M_t); then M = max_t M_t and
+    S = sum_t S_t * exp_c(M_t - M) (left to right), so that a row is read
+    once; p_j = exp_c(x_j - M) / S;
   * sampling: inverse CDF over the same hierarchy (tile sums, then thread
     sums, then the thread's 16 elements), each level scanned left to right
     with float32 running sums; a level where rounding leaves the target
@@ -133,11 +137,23 @@ def scaled_logits(logits, temperature):
 
 
 def row_stats(x):
-    """(max, canonical sum of exp_c(x - max)) of one logits row (already / T)."""
-    M = f32(x.max())
-    e = exp_c((x - M).astype(f32))
-    _, _, R = canon_partials(e)
-    return M, f32(R)
+    """(max M, normaliser S) of one logits row (already / T), tile by tile."""
+    x = np.asarray(x, dtype=f32)
+    V = x.shape[-1]
+    T = (V + TILE - 1) // TILE
+    pad = np.full(T * TILE, -np.inf, f32)
+    pad[:V] = x
+    tiles = pad.reshape(T, TILE)
+    Mt = tiles.max(axis=1).astype(f32)
+    with np.errstate(invalid="ignore"):
+        e = exp_c((tiles - Mt[:, None]).astype(f32))
+    e = np.where(np.isfinite(tiles), e, f32(0.0)).astype(f32)
+    _, St, _ = canon_partials(e.reshape(T * TILE)[:V])
+    M = f32(Mt.max())
+    S = f32(0.0)
+    for t in range(T):
+        S = f32(S + f32(St[t] * exp_c(f32(Mt[t] - M))))
+    return M, S
 
 
 def probs(x, M, S):
