@@ -53,8 +53,14 @@ def parse():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--workload", choices=["decode", "prefill", "verify"], default="decode",
-                    help="decode = config 5 (the bench line); prefill = config 3; verify = config 4 (1 GPU)")
+    ap.add_argument("--workload", choices=["decode", "prefill", "verify", "engine"], default="decode",
+                    help="decode = config 5 (the bench line); prefill = config 3; verify = config 4; "
+                         "engine = config 2 through nano-vLLM's own engine (1 GPU)")
+    ap.add_argument("--engine-attn", choices=["b200", "flash_attn"], default="b200",
+                    help="engine workload: this package's Attention, or the reference's stock flash-attn path")
+    ap.add_argument("--engine-model", choices=["qwen3-0.6b", "qwen3-8b"], default="qwen3-0.6b")
+    ap.add_argument("--engine-requests", type=int, default=256)
+    ap.add_argument("--gpu-mem", type=float, default=0.5, help="engine KV-cache share of GPU memory")
     ap.add_argument("--batch", type=int, default=BATCH,
                     help="sequences in the batch (profiling runs use a smaller batch; the bench line uses 512)")
     return ap.parse_args()
@@ -392,6 +398,97 @@ def run_verify(args, pkg, torch, dev):
         "clocks": clk.summary()}), flush=True)
 
 
+QWEN3 = {
+    "qwen3-0.6b": dict(hidden_size=1024, intermediate_size=3072, num_hidden_layers=28, num_attention_heads=16,
+                       num_key_value_heads=8, tie_word_embeddings=True),
+    "qwen3-8b": dict(hidden_size=4096, intermediate_size=12288, num_hidden_layers=36, num_attention_heads=32,
+                     num_key_value_heads=8, tie_word_embeddings=False),
+}
+
+
+def _qwen3_config_dir(name):
+    """A Hugging Face config directory for a randomly initialised Qwen3 (no checkpoint here)."""
+    import tempfile
+    cfg = dict(QWEN3[name], architectures=["Qwen3ForCausalLM"], model_type="qwen3", head_dim=128, vocab_size=151936,
+               max_position_embeddings=40960, rms_norm_eps=1e-6, rope_theta=1000000.0, attention_bias=False,
+               hidden_act="silu", torch_dtype="bfloat16", dtype="bfloat16", bos_token_id=151643,
+               eos_token_id=151645)
+    d = tempfile.mkdtemp(prefix="b200_qwen3_")
+    with open(os.path.join(d, "config.json"), "w") as f:
+        json.dump(cfg, f)
+    return d
+
+
+class _IdTokenizer:
+    """Prompts are token ids and generation ignores EOS, so no vocabulary is needed."""
+    eos_token_id = -1
+
+    @classmethod
+    def from_pretrained(cls, *a, **k):
+        return cls()
+
+    def encode(self, text):
+        return [ord(c) % 151936 for c in text]
+
+    def decode(self, ids):
+        return ""
+
+
+def _random_init(model, path):
+    """Stands in for nanovllm.utils.loader.load_model: N(0, 0.02) weights, unit norms."""
+    import torch
+    g = torch.Generator(device="cuda").manual_seed(0)
+    with torch.no_grad():
+        for _, prm in model.named_parameters():
+            if prm.dim() == 1:
+                prm.fill_(1.0)
+            else:
+                prm.normal_(0.0, 0.02, generator=g)
+
+
+def run_engine(args, pkg):
+    """Config 2 through nano-vLLM's own LLM engine (scheduler, block manager,
+    prefix cache, CUDA-graph decode): 256 requests, prompt and output lengths
+    U[100, 1024], prompt ids uniform over the vocabulary, temperature 0.6,
+    ignore_eos; output tokens / wall time of generate() as in the reference
+    bench.py:21-27.  Weights are random (no checkpoint is available)."""
+    import torch
+    sys.path.insert(0, os.path.join(ROOT, "baseline", "_ref"))
+    import nanovllm.engine.llm_engine as le
+    import nanovllm.engine.model_runner as mr
+    le.AutoTokenizer = _IdTokenizer
+    mr.load_model = _random_init
+    if args.engine_attn == "b200":
+        pkg.install()
+    from nanovllm import LLM, SamplingParams
+    path = _qwen3_config_dir(args.engine_model)
+    t_init = time.perf_counter()
+    llm = LLM(path, enforce_eager=False, max_model_len=4096, gpu_memory_utilization=args.gpu_mem)
+    t_init = time.perf_counter() - t_init
+    rng = np.random.default_rng(0)
+    n = args.engine_requests
+    prompts = [rng.integers(0, 151936, size=int(rng.integers(100, 1025))).tolist() for _ in range(n)]
+    sps = [SamplingParams(temperature=0.6, ignore_eos=True, max_tokens=int(rng.integers(100, 1025))) for _ in range(n)]
+    # Warm-up with varied prompt lengths and batch sizes, so that torch.compile's
+    # shape specialisations of the reference's other layers happen before timing.
+    llm.generate([p[:int(k)] for p, k in zip(prompts[:24], np.linspace(100, 1024, 24))],
+                 SamplingParams(temperature=0.6, ignore_eos=True, max_tokens=24), use_tqdm=False)
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        t = time.perf_counter()
+        out = llm.generate(prompts, sps, use_tqdm=False)
+        t = time.perf_counter() - t
+    total = sum(sp.max_tokens for sp in sps)
+    assert all(len(o["token_ids"]) == sp.max_tokens for o, sp in zip(out, sps))
+    print(json.dumps({
+        "metric": "e2e output tokens/s (nano-vLLM engine, config 2)", "value": round(total / t, 1), "unit": "tok/s",
+        "n_gpus": 1, "higher_is_better": True, "dtype": "bf16", "data": "synthetic prompts, random-init weights",
+        "attention": args.engine_attn, "vs_baseline": round(total / t / 1434.13, 3),
+        "config": {"workload": f"config2: {args.engine_model}, {n} requests, in/out U[100,1024], T=0.6, ignore_eos",
+                   "output_tokens": total, "seconds": round(t, 3), "engine_init_s": round(t_init, 1),
+                   "gpu_memory_utilization": args.gpu_mem},
+        "clocks": clk.summary()}), flush=True)
+
+
 def _peak_tflops():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -419,6 +516,10 @@ def main():
     pkg = __graft_entry__.load_package()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    if args.workload == "engine":
+        assert world == 1, "the engine workload runs on one GPU"
+        run_engine(args, pkg)
+        return
     if args.workload != "decode":
         assert world == 1, "the prefill / verify workloads run on one GPU"
         (run_prefill if args.workload == "prefill" else run_verify)(args, pkg, torch, dev)
