@@ -92,14 +92,26 @@ def measured_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def profiled_traffic():
-    """DRAM bytes per paged-attention launch from the committed ncu summary (or None)."""
+def profiled_traffic(bytes_per_launch):
+    """DRAM bytes per paged-attention launch: the DRAM-traffic / algorithmic-bytes
+    ratio from the committed ncu summary times this launch's algorithmic bytes
+    (or None without a summary)."""
     p = os.path.join(ROOT, "profiles", "paged_attention_config5.md")
     try:
-        m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", open(p).read())
-        return float(m.group(1)) if m else None
+        m = re.search(r"dram_traffic_ratio:\s*([0-9.eE+]+)", open(p).read())
+        return round(float(m.group(1)) * bytes_per_launch) if m else None
     except OSError:
         return None
+
+
+def _all_host_threads():
+    """BLAS thread limit raised to every host core (torchrun sets OMP_NUM_THREADS=1)."""
+    try:
+        from threadpoolctl import threadpool_limits
+        return threadpool_limits(limits=os.cpu_count() or 1)
+    except Exception:
+        import contextlib
+        return contextlib.nullcontext()
 
 
 class ClockSampler:
@@ -507,7 +519,8 @@ def main():
         world = args.gpus if "WORLD_SIZE" not in os.environ else world
     assert HKV_TOTAL % world == 0, f"{world} GPUs do not divide {HKV_TOTAL} kv heads"
     if args.impl == "reference":
-        run_reference(args, rank, world)
+        with _all_host_threads():
+            run_reference(args, rank, world)
         return
 
     import torch
@@ -663,14 +676,15 @@ def main():
                         "ms_per_step": round(e2e_ms, 5), "api": "Attention.forward (decode), pinned host buffers"},
                 "roofline": {"bound": "hbm", "kernel": "paged_attention_kernel", "achieved": round(achieved, 1),
                              "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
-                             "traffic": profiled_traffic(), "bytes_per_launch": int(dec_b),
+                             "traffic": profiled_traffic(dec_b), "bytes_per_launch": int(dec_b),
                              "us_per_launch": round(kern_ms * 1e3, 2)},
                 "gpu_launches": 2 * args.steps,
                 "clocks": clk.summary()}
         if allreduce:
             line["allreduce"] = allreduce
         if not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(ctx, hq, hkv, args.cpu_seconds)
+            with _all_host_threads():
+                line["cpu_baseline"] = cpu_baseline(ctx, hq, hkv, args.cpu_seconds)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier(device_ids=[local])
