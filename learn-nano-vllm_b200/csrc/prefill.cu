@@ -3,37 +3,37 @@
 // nanovllm/layers/attention.py:64-70, with or without a block table (prefix
 // caching / chunked prefill reads keys from the paged cache).
 //
-// One CTA computes one 128-query tile of one query head.  Warp roles:
-//   warp 0  producer: TMA loads (no multicast) of the Q tile once and of
-//           128-key K and V tiles into a 2-stage ring (64 KiB per stage),
-//           all as 64-dim x 128-row boxes with 128-byte swizzle;
-//   warp 1  MMA issuer (one thread): S_j = Q K_j^T into one of two TMEM
-//           buffers (SS MMA, M = N = 128, K-major operands), and
-//           O += P_j V_j with P_j read from tensor memory (TS MMA, V as an
-//           MN-major operand); completions are signalled with tcgen05.commit;
-//   warps 2-5 softmax: one thread per query row (TMEM lane = row) loads its
-//           S row, applies the bottom-right causal mask, keeps the running
-//           max and sum, writes P_j as bf16 over S_j in tensor memory, and
-//           rescales the O row in tensor memory when the max grew by more
-//           than 2^8 (lazy rescaling keeps exponents bounded, the sum uses
-//           the same stale max, so the result is exact).
-// S_{j+1} is issued before PV_j, so the tensor core computes the next
-// scores while the softmax warps work on the current tile.  TMEM: S0 at
-// columns 0-127, S1 at 128-255, O at 256-383 (512 allocated).
+// One CTA computes two 128-query tiles (A = rows 0-127, B = rows 128-255 of
+// a 256-row block) of one query head; both share every K/V tile.  Warp roles:
+//   warp 0    producer: TMA loads (no multicast) of both Q tiles once and of
+//             128-key K and V tiles into a 2-stage ring (64 KiB per stage),
+//             all as 64-dim x 128-row boxes with 128-byte swizzle;
+//   warp 1    MMA issuer (one thread) and tensor-memory owner;
+//   warps 2-5 softmax of tile A, warps 6-9 softmax of tile B: one thread per
+//             query row (TMEM lane = row).
+// Tensor memory: S_A cols 0-127, S_B 128-255, O_A 256-383, O_B 384-511.  The
+// MMA order per key tile j is PV_A(j-1) S_A(j) PV_B(j-1) S_B(j) (ping-pong):
+// while one warpgroup turns S(j) into P(j), the tensor core works on the
+// other tile.  S = Q K^T is an SS MMA (M = N = 128, K-major operands); the
+// softmax writes P as bf16 over its S columns and O += P V reads P from
+// tensor memory (TS MMA) with V as an MN-major operand.  The softmax is two
+// passes over its TMEM row (max, then exp / pack / store by 32-column chunk)
+// and rescales its O row in tensor memory only when the running max grew by
+// more than 2^8 (lazy rescaling; the sum uses the same stale max, so the
+// result is exact).
 #include "common.cuh"
 #include "tcgen05.cuh"
 
 namespace b200 {
 namespace pf {
 
-constexpr int kBM = 128;  // queries per tile
+constexpr int kBM = 128;  // queries per tile (two tiles per CTA)
 constexpr int kBN = 128;  // keys per tile
 constexpr int kD = 128;
 constexpr int kHalf = kBM * 128;  // one 64-dim half of a 128-row tile: 16 KiB
 constexpr int kStages = 2;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO = 256;
 constexpr float kRescaleLog2 = 8.0f;
 
 struct Params {
@@ -43,17 +43,16 @@ struct Params {
     const int32_t* cu_k;
     const int32_t* block_tables;
     int32_t bt_stride, block_size, num_blocks;
-    int32_t num_seqs, hq, hkv, group, q_tiles;
+    int32_t num_seqs, hq, hkv, group, q_blocks;
     float scale_log2;
 };
 
 struct Smem {
-    uint8_t q[2][kHalf];
+    uint8_t q[2][2][kHalf];         // [tile A/B][dim half]
     uint8_t kv[kStages][4][kHalf];  // K lo, K hi, V lo, V hi
     uint64_t q_full;
     uint64_t kv_full[kStages], kv_empty[kStages];
-    uint64_t s_full[2], p_ready[2];
-    uint64_t o_done;
+    uint64_t s_full[2], p_ready[2], o_done[2];  // per tile A/B
     uint64_t drain;
     uint32_t tmem_base;
     int32_t err;
@@ -68,6 +67,14 @@ __device__ __forceinline__ bool wait_or_flag(uint64_t* bar, uint32_t parity, Sme
     return false;
 }
 
+// Number of 128-key tiles that rows [r0, r1) of a sequence (lq queries, lk keys) may see.
+__device__ __forceinline__ int key_tiles(int r0, int r1, int lq, int lk) {
+    if (r0 >= lq) return 0;
+    const int last = min(r1, lq) - 1;
+    const int nkeys = max(0, min(lk, last + (lk - lq) + 1));
+    return (nkeys + kBN - 1) / kBN;
+}
+
 template <bool BF16>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtensorMap tmq,
@@ -77,19 +84,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
     const int h = blockIdx.x;
-    const int tile = p.q_tiles - 1 - int(blockIdx.y);  // longest (latest) tiles first
+    const int blk_q = p.q_blocks - 1 - int(blockIdx.y);  // longest (latest) rows first
     const int s = blockIdx.z;
     const int q0 = p.cu_q[s], lq = p.cu_q[s + 1] - q0;
     const int k0 = p.cu_k[s], lk = p.cu_k[s + 1] - k0;
-    const int row0 = tile * kBM;
+    const int row0 = blk_q * 2 * kBM;
     if (row0 >= lq) return;  // uniform across the CTA
-    const int last_row = min(row0 + kBM, lq) - 1;
-    const int nkeys = max(0, min(lk, last_row + (lk - lq) + 1));  // keys any row of the tile may see
-    const int ntiles = (nkeys + kBN - 1) / kBN;
+    const int nt[2] = {key_tiles(row0, row0 + kBM, lq, lk), key_tiles(row0 + kBM, row0 + 2 * kBM, lq, lk)};
+    const int ntiles = max(nt[0], nt[1]);
+    const bool has_b = row0 + kBM < lq;
     const int kvh = h / p.group;
 
     if (ntiles == 0) {  // no visible key for any row: zero output
-        for (int i = tid; i < (last_row - row0 + 1) * (kD / 8); i += kThreads) {
+        const int rows = min(2 * kBM, lq - row0);
+        for (int i = tid; i < rows * (kD / 8); i += kThreads) {
             const int r = row0 + i / (kD / 8), c = i % (kD / 8);
             reinterpret_cast<uint4*>(p.out + int64_t(q0 + r) * p.out_stride + h * kD)[c] = make_uint4(0, 0, 0, 0);
         }
@@ -105,8 +113,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 2; ++i) {
             mbar_init(&sm.s_full[i], 1);
             mbar_init(&sm.p_ready[i], 128);
+            mbar_init(&sm.o_done[i], 1);
         }
-        mbar_init(&sm.o_done, 1);
         mbar_init(&sm.drain, 1);
         sm.err = 0;
         fence_mbar_init();
@@ -128,9 +136,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             prefetch_tmap(&tmv);
             const uint64_t pol_q = l2_policy_evict_first();
             const uint64_t pol_kv = l2_policy_evict_last();  // K/V tiles are re-read by the group's q heads
-            mbar_arrive_expect_tx(&sm.q_full, 2 * kHalf);
-            tma_load_2d(sm.q[0], &tmq, h * kD, q0 + row0, &sm.q_full, pol_q);
-            tma_load_2d(sm.q[1], &tmq, h * kD + 64, q0 + row0, &sm.q_full, pol_q);
+            mbar_arrive_expect_tx(&sm.q_full, (has_b ? 4 : 2) * kHalf);
+            for (int t = 0; t < (has_b ? 2 : 1); ++t) {
+                tma_load_2d(sm.q[t][0], &tmq, h * kD, q0 + row0 + t * kBM, &sm.q_full, pol_q);
+                tma_load_2d(sm.q[t][1], &tmq, h * kD + 64, q0 + row0 + t * kBM, &sm.q_full, pol_q);
+            }
             const int32_t* bt = p.block_tables ? p.block_tables + int64_t(s) * p.bt_stride : nullptr;
             int filled = 0;
             for (int j = 0; j < ntiles; ++j) {
@@ -171,70 +181,91 @@ __global__ void __launch_bounds__(kThreads, 1)
             constexpr uint32_t idPV = tc::idesc_f16<BF16>(kBM, kD, false, true);
             bool ok = wait_or_flag(&sm.q_full, 0, sm);
             tc::fence_after_sync();
-            const uint32_t qa = smem_u32(sm.q[0]);
-            auto issue_pv = [&](int j) {
-                const int sb = j & 1, st = j % kStages;
-                if (!wait_or_flag(&sm.p_ready[sb], (j >> 1) & 1, sm)) return false;
-                tc::fence_after_sync();
-                const uint32_t va = smem_u32(sm.kv[st][2]);
-#pragma unroll
-                for (int kk = 0; kk < kBN / 16; ++kk) {
-                    // V is MN-major: 16 keys = two 8-row swizzle atoms (SBO 1024 B); the
-                    // second 64 dims live in the V-hi half (LBO = kHalf).
-                    const uint64_t bdesc = tc::smem_desc_sw128(va + kk * 16 * 128, kHalf, 1024);
-                    tc::mma_ts(tmem + kColO, tmem + (sb ? kColS1 : kColS0) + kk * 8, bdesc, idPV,
-                               (j > 0 || kk > 0) ? 1u : 0u);
-                }
-                tc::commit(&sm.kv_empty[st]);
-                tc::commit(&sm.o_done);
-                return true;
-            };
-            for (int j = 0; ok && j < ntiles; ++j) {
-                const int sb = j & 1, st = j % kStages;
-                if (!wait_or_flag(&sm.kv_full[st], (j / kStages) & 1, sm)) { ok = false; break; }
-                tc::fence_after_sync();
-                const uint32_t ka = smem_u32(sm.kv[st][0]);
+            auto issue_s = [&](int t, int j) {
+                const uint32_t qa = smem_u32(sm.q[t][0]);
+                const uint32_t ka = smem_u32(sm.kv[j % kStages][0]);
 #pragma unroll
                 for (int kk = 0; kk < kD / 16; ++kk) {
                     // K-major operands: 16 dims = 32 bytes inside a 128-byte swizzled row
                     const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
-                    const uint64_t adesc = tc::smem_desc_sw128(qa + off, 16, 1024);
-                    const uint64_t bdesc = tc::smem_desc_sw128(ka + off, 16, 1024);
-                    tc::mma_ss(tmem + (sb ? kColS1 : kColS0), adesc, bdesc, idS, kk > 0 ? 1u : 0u);
+                    tc::mma_ss(tmem + t * 128, tc::smem_desc_sw128(qa + off, 16, 1024),
+                               tc::smem_desc_sw128(ka + off, 16, 1024), idS, kk > 0 ? 1u : 0u);
                 }
-                tc::commit(&sm.s_full[sb]);
-                if (j > 0 && !issue_pv(j - 1)) { ok = false; break; }
+                tc::commit(&sm.s_full[t]);
+            };
+            auto issue_pv = [&](int t, int j) {
+                if (!wait_or_flag(&sm.p_ready[t], j & 1, sm)) return false;
+                tc::fence_after_sync();
+                const uint32_t va = smem_u32(sm.kv[j % kStages][2]);
+#pragma unroll
+                for (int kk = 0; kk < kBN / 16; ++kk) {
+                    // V is MN-major: 16 keys = two 8-row swizzle atoms (SBO 1024 B); the
+                    // second 64 dims live in the V-hi half (LBO = kHalf).
+                    tc::mma_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8,
+                               tc::smem_desc_sw128(va + kk * 16 * 128, kHalf, 1024), idPV,
+                               (j > 0 || kk > 0) ? 1u : 0u);
+                }
+                tc::commit(&sm.o_done[t]);
+                return true;
+            };
+            for (int j = 0; ok && j < ntiles; ++j) {
+                if (!wait_or_flag(&sm.kv_full[j % kStages], (j / kStages) & 1, sm)) { ok = false; break; }
+                tc::fence_after_sync();
+                // tile A: PV(j-1) frees S_A before S_A(j) overwrites it (in-order tensor pipe)
+                if (j < nt[0]) {
+                    if (j > 0 && !issue_pv(0, j - 1)) { ok = false; break; }
+                    issue_s(0, j);
+                } else if (j == nt[0] && j > 0) {
+                    if (!issue_pv(0, j - 1)) { ok = false; break; }
+                }
+                if (j < nt[1]) {
+                    if (j > 0 && !issue_pv(1, j - 1)) { ok = false; break; }
+                    issue_s(1, j);
+                }
+                if (j > 0) tc::commit(&sm.kv_empty[(j - 1) % kStages]);  // both PVs of tile j-1 issued
             }
-            if (ok) issue_pv(ntiles - 1);
+            if (ok) {
+                if (nt[0] == ntiles) ok = issue_pv(0, ntiles - 1);
+                if (ok && nt[1] == ntiles) ok = issue_pv(1, ntiles - 1);
+                tc::commit(&sm.kv_empty[(ntiles - 1) % kStages]);
+            }
             // Wait (bounded) for every MMA issued above before the tensor memory is freed.
             tc::commit(&sm.drain);
             mbar_wait(&sm.drain, 0);
         }
     } else {
         // ------------------------------------------------------------ softmax / epilogue
-        const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31 belong to this warp
+        const int t = warp >= 6 ? 1 : 0;  // query tile of this warpgroup
+        const int quarter = warp & 3;     // TMEM lanes 32*quarter .. +31 belong to this warp
         const int r = quarter * 32 + lane;
         const uint32_t lane_addr = uint32_t(quarter * 32) << 16;
-        const int qrow = row0 + r;
+        const uint32_t s_col = tmem + lane_addr + t * 128;
+        const uint32_t o_col = tmem + lane_addr + 256 + t * 128;
+        const int qrow = row0 + t * kBM + r;
         const int limit = qrow < lq ? qrow + (lk - lq) : -1;  // last visible key of this row
         const float sl2 = p.scale_log2;
+        const int my_tiles = nt[t];
         float m = -INFINITY, l = 0.f;
         bool ok = true;
-        for (int j = 0; j < ntiles; ++j) {
-            const int sb = j & 1;
-            if (!wait_or_flag(&sm.s_full[sb], (j >> 1) & 1, sm)) { ok = false; break; }
+        for (int j = 0; j < my_tiles; ++j) {
+            if (!wait_or_flag(&sm.s_full[t], j & 1, sm)) { ok = false; break; }
             tc::fence_after_sync();
-            const uint32_t sa = tmem + lane_addr + (sb ? kColS1 : kColS0);
-            float v[kBN];
-#pragma unroll
-            for (int c = 0; c < kBN / 32; ++c) tc::tmem_ld32(sa + c * 32, *reinterpret_cast<float(*)[32]>(&v[c * 32]));
-            tc::tmem_wait_ld();
             const int kbase = j * kBN;
+            const bool full_row = kbase + kBN - 1 <= limit;  // no masking needed in this tile
+            // pass 1: row max
             float mx = -INFINITY;
+#pragma unroll 1
+            for (int c = 0; c < kBN / 32; ++c) {
+                float v[32];
+                tc::tmem_ld32(s_col + c * 32, v);
+                tc::tmem_wait_ld();
+                float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-            for (int c = 0; c < kBN; ++c) {
-                if (kbase + c > limit) v[c] = -INFINITY;
-                mx = fmaxf(mx, v[c]);
+                for (int e = 0; e < 32; ++e) {
+                    const float x = (full_row || kbase + c * 32 + e <= limit) ? v[e] : -INFINITY;
+                    m4[e & 3] = fmaxf(m4[e & 3], x);
+                }
+                mx = fmaxf(mx, fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])));
             }
             // Lazy rescale: keep the old max unless the new one exceeds it by 2^8.
             float alpha = 1.f;
@@ -245,40 +276,47 @@ __global__ void __launch_bounds__(kThreads, 1)
                 m = mx;
             }
             const float msl = m == -INFINITY ? 0.f : m * sl2;
-            float sum = 0.f;
-            uint32_t pk[kBN / 2];
+            // pass 2: P = exp2(S*scale - m) as bf16 over the S columns, row sum
+            float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+            for (int c = 0; c < kBN / 32; ++c) {
+                float v[32];
+                tc::tmem_ld32(s_col + c * 32, v);
+                tc::tmem_wait_ld();
+                uint32_t pk[16];
 #pragma unroll
-            for (int c = 0; c < kBN; c += 2) {
-                const float a = fast_exp2(fmaf(v[c], sl2, -msl));
-                const float b = fast_exp2(fmaf(v[c + 1], sl2, -msl));
-                sum += a + b;
-                pk[c / 2] = pack2<BF16>(a, b);
+                for (int e = 0; e < 32; e += 2) {
+                    const bool in0 = full_row || kbase + c * 32 + e <= limit;
+                    const bool in1 = full_row || kbase + c * 32 + e + 1 <= limit;
+                    const float a = in0 ? fast_exp2(fmaf(v[e], sl2, -msl)) : 0.f;
+                    const float b = in1 ? fast_exp2(fmaf(v[e + 1], sl2, -msl)) : 0.f;
+                    sum4[(e >> 1) & 3] += a + b;
+                    pk[e / 2] = pack2<BF16>(a, b);
+                }
+                // P chunk c (32 keys) occupies 16 TMEM columns at s_col + 16c
+                tc::tmem_st16(s_col + c * 16, pk);
             }
-            l = fmaf(l, alpha, sum);
-            const uint32_t pa = tmem + lane_addr + (sb ? kColS1 : kColS0);
-            tc::tmem_st32(pa, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
-            tc::tmem_st32(pa + 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
+            l = fmaf(l, alpha, (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
             if (rescale && j > 0) {
-                // O must hold PV_{j-1} before it is scaled.
-                if (!wait_or_flag(&sm.o_done, (j - 1) & 1, sm)) { ok = false; break; }
+                // O must hold PV(j-1) before it is scaled.
+                if (!wait_or_flag(&sm.o_done[t], (j - 1) & 1, sm)) { ok = false; break; }
                 tc::fence_after_sync();
 #pragma unroll 1
                 for (int c = 0; c < kD / 32; ++c) {
                     float o[32];
-                    tc::tmem_ld32(tmem + lane_addr + kColO + c * 32, o);
+                    tc::tmem_ld32(o_col + c * 32, o);
                     tc::tmem_wait_ld();
                     uint32_t u[32];
 #pragma unroll
                     for (int e = 0; e < 32; ++e) u[e] = __float_as_uint(o[e] * alpha);
-                    tc::tmem_st32(tmem + lane_addr + kColO + c * 32, u);
+                    tc::tmem_st32(o_col + c * 32, u);
                 }
             }
             tc::tmem_wait_st();
-            // Cache rows past the keys of this sequence may hold NaN bits; P is 0
-            // there but 0 * NaN is NaN, so clear those V rows before PV reads them.
-            if (kbase + kBN > lk) {
-                const int key = kbase + r;
-                if (key >= lk) {
+            // Cache rows past this sequence's keys may hold NaN bits; P is 0 there but
+            // 0 * NaN is NaN, so the first tile to use the stage clears those V rows.
+            if (kbase + kBN > lk && (t == 0 || j >= nt[0])) {
+                if (kbase + r >= lk) {
                     uint4* v0 = reinterpret_cast<uint4*>(sm.kv[j % kStages][2] + r * 128);
                     uint4* v1 = reinterpret_cast<uint4*>(sm.kv[j % kStages][3] + r * 128);
 #pragma unroll
@@ -287,17 +325,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                 fence_proxy_async_smem();
             }
             tc::fence_before_sync();
-            mbar_arrive(&sm.p_ready[sb]);
+            mbar_arrive(&sm.p_ready[t]);
         }
         // ---- epilogue: O / l -> bf16, one query row per thread ----
-        if (ok && wait_or_flag(&sm.o_done, (ntiles - 1) & 1, sm)) {
+        if (ok && my_tiles > 0 && wait_or_flag(&sm.o_done[t], (my_tiles - 1) & 1, sm)) {
             tc::fence_after_sync();
             const float inv = l > 0.f ? 1.f / l : 0.f;
             uint4* dst = reinterpret_cast<uint4*>(p.out + int64_t(q0 + qrow) * p.out_stride + h * kD);
 #pragma unroll 1
             for (int c = 0; c < kD / 32; ++c) {
                 float o[32];
-                tc::tmem_ld32(tmem + lane_addr + kColO + c * 32, o);
+                tc::tmem_ld32(o_col + c * 32, o);
                 tc::tmem_wait_ld();
                 if (qrow < lq) {
 #pragma unroll
@@ -311,6 +349,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
             }
+        } else if (my_tiles == 0 && qrow < lq) {
+            // rows of tile B that see no key (possible only when lk < lq)
+            uint4* dst = reinterpret_cast<uint4*>(p.out + int64_t(q0 + qrow) * p.out_stride + h * kD);
+            for (int c = 0; c < kD / 8; ++c) dst[c] = make_uint4(0, 0, 0, 0);
         }
     }
 
@@ -356,9 +398,9 @@ extern "C" int32_t b200_varlen_prefill(void* out, const void* q, int64_t q_strid
         B200_REQUIRE(block_table_stride > 0, "varlen_prefill: block_table_stride %d", block_table_stride);
         B200_REQUIRE(total_k_rows % block_size == 0, "varlen_prefill: cache rows %d not whole blocks", total_k_rows);
     }
-    const int q_tiles = (max_seqlen_q + kBM - 1) / kBM;
-    if (q_tiles > 65535 || num_seqs > 65535)
-        return fail(B200_ERR_UNSUPPORTED, "varlen_prefill: %d query tiles x %d sequences", q_tiles, num_seqs);
+    const int q_blocks = (max_seqlen_q + 2 * kBM - 1) / (2 * kBM);
+    if (q_blocks > 65535 || num_seqs > 65535)
+        return fail(B200_ERR_UNSUPPORTED, "varlen_prefill: %d query blocks x %d sequences", q_blocks, num_seqs);
     const bool bf16 = dtype == B200_BF16;
     // The tensor maps span exactly the caller's q / k / v rows, so a tile that
     // runs past the last token reads the TMA fill value (zero), never memory
@@ -388,13 +430,13 @@ extern "C" int32_t b200_varlen_prefill(void* out, const void* q, int64_t q_strid
     prm.hq = num_heads;
     prm.hkv = num_kv_heads;
     prm.group = num_heads / num_kv_heads;
-    prm.q_tiles = q_tiles;
+    prm.q_blocks = q_blocks;
     prm.scale_log2 = softmax_scale * 1.4426950408889634f;
 
     const int smem = int(sizeof(Smem)) + 1024;
     const void* fn = bf16 ? (const void*)prefill_kernel<true> : (const void*)prefill_kernel<false>;
     ensure_smem_attr(fn, smem);
-    const dim3 grid(num_heads, q_tiles, num_seqs);
+    const dim3 grid(num_heads, q_blocks, num_seqs);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (bf16) prefill_kernel<true><<<grid, kThreads, smem, st>>>(prm, tmq, tmk, tmv);
     else prefill_kernel<false><<<grid, kThreads, smem, st>>>(prm, tmq, tmk, tmv);
