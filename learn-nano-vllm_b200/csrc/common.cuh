@@ -78,14 +78,19 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// Potentially blocking test: with a suspend-time hint the hardware parks the
+// thread until the phase completes (or the hint, in ns, expires) and wakes it
+// promptly on completion; without one it may sleep for a fixed period.
+constexpr uint32_t kTryWaitSuspendNs = 1000000;  // 1 ms per try; callers bound the total
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(kTryWaitSuspendNs)
         : "memory");
     return ok != 0;
 }
@@ -174,6 +179,21 @@ __device__ __forceinline__ float fast_exp2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+
+// 2^x on the FMA pipe (relieves the MUFU unit that fast_exp2 uses):
+// x = n + f with n = rint(x) (magic-constant rounding) and f in [-0.5, 0.5];
+// 2^f by a cubic least-squares fit (max relative error 1.8e-4 for
+// x in [-125, 8]); 2^n added to the exponent bits.  Inputs below -125 clamp.
+__device__ __forceinline__ float exp2_poly(float x) {
+    x = fmaxf(x, -125.f);
+    const float t = x + 12582912.f;  // 1.5 * 2^23: rint(x) lands in the low mantissa bits
+    const float n = t - 12582912.f;
+    const float f = x - n;
+    float p = fmaf(f, 0x1.bf4e00p-5f, 0x1.ef75eap-3f);
+    p = fmaf(f, p, 0x1.62fa60p-1f);
+    p = fmaf(f, p, 1.0f);
+    return __int_as_float(__float_as_int(p) + ((__float_as_int(t) - 0x4B400000) << 23));
 }
 
 __device__ __forceinline__ float fast_log2(float x) {

@@ -3,8 +3,12 @@
 // nanovllm/layers/attention.py:64-70, with or without a block table (prefix
 // caching / chunked prefill reads keys from the paged cache).
 //
-// One CTA computes two 128-query tiles (A = rows 0-127, B = rows 128-255 of
-// a 256-row block) of one query head; both share every K/V tile.  Warp roles:
+// Persistent CTAs (one per SM) walk work units -- two 128-query tiles (A =
+// rows 0-127, B = rows 128-255 of a 256-row block) of one query head of one
+// sequence -- heaviest first; both tiles share every K/V tile.  Tensor memory
+// is allocated once; the K/V ring and every barrier phase run on across
+// units, the next unit's Q loads as soon as the last S MMA of the current one
+// completes, and its MMAs overlap the current unit's epilogue.  Warp roles:
 //   warp 0    producer: TMA loads (no multicast) of both Q tiles once and of
 //             128-key K and V tiles into a 2-stage ring (64 KiB per stage),
 //             all as 64-dim x 128-row boxes with 128-byte swizzle;
@@ -21,6 +25,8 @@
 // and rescales its O row in tensor memory only when the running max grew by
 // more than 2^8 (lazy rescaling; the sum uses the same stale max, so the
 // result is exact).
+#include <climits>
+
 #include "common.cuh"
 #include "tcgen05.cuh"
 
@@ -31,7 +37,8 @@ constexpr int kBM = 128;  // queries per tile (two tiles per CTA)
 constexpr int kBN = 128;  // keys per tile
 constexpr int kD = 128;
 constexpr int kHalf = kBM * 128;  // one 64-dim half of a 128-row tile: 16 KiB
-constexpr int kStages = 2;
+constexpr int kKStages = 3;  // K tiles are released after S, so they can run further ahead
+constexpr int kVStages = 2;  // V tiles are released after PV
 constexpr int kThreads = 320;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleLog2 = 8.0f;
@@ -48,10 +55,12 @@ struct Params {
 };
 
 struct Smem {
-    uint8_t q[2][2][kHalf];         // [tile A/B][dim half]
-    uint8_t kv[kStages][4][kHalf];  // K lo, K hi, V lo, V hi
-    uint64_t q_full;
-    uint64_t kv_full[kStages], kv_empty[kStages];
+    uint8_t q[2][2][kHalf];          // [tile A/B][dim half]
+    uint8_t k[kKStages][2][kHalf];   // [stage][dim half]
+    uint8_t v[kVStages][2][kHalf];
+    uint64_t q_full, q_empty;
+    uint64_t k_full[kKStages], k_empty[kKStages];
+    uint64_t v_full[kVStages], v_empty[kVStages];
     uint64_t s_full[2], p_ready[2], o_done[2];  // per tile A/B
     uint64_t drain;
     uint32_t tmem_base;
@@ -75,6 +84,94 @@ __device__ __forceinline__ int key_tiles(int r0, int r1, int lq, int lk) {
     return (nkeys + kBN - 1) / kBN;
 }
 
+// One work unit: a 256-row query block (tiles A and B) of one head of one sequence.
+struct Unit {
+    int s, h, q0, lq, k0, lk, row0, nt[2], ntiles;
+    bool has_b;
+};
+
+// Units are numbered heaviest first (later query blocks see more keys), then by
+// sequence and head; returns false for blocks past the sequence's queries.
+// CTA c takes the units at positions i with snake(i) == c, where positions run
+// c, then 2G-1-c, then 2G+c, ... (boustrophedon), which balances the static
+// assignment of units of decreasing cost.
+__device__ __forceinline__ int unit_at(int k, int cta, int G) {
+    return (k & 1) ? (k + 1) * G - 1 - cta : k * G + cta;
+}
+__device__ __forceinline__ bool load_unit(const Params& p, int u, Unit& w) {
+    const int per = p.num_seqs * p.hq;
+    const int qb = p.q_blocks - 1 - u / per;
+    const int rem = u - (u / per) * per;
+    w.s = rem / p.hq;
+    w.h = rem - w.s * p.hq;
+    w.q0 = p.cu_q[w.s];
+    w.lq = p.cu_q[w.s + 1] - w.q0;
+    w.row0 = qb * 2 * kBM;
+    if (w.row0 >= w.lq) return false;
+    w.k0 = p.cu_k[w.s];
+    w.lk = p.cu_k[w.s + 1] - w.k0;
+    w.nt[0] = key_tiles(w.row0, w.row0 + kBM, w.lq, w.lk);
+    w.nt[1] = key_tiles(w.row0 + kBM, w.row0 + 2 * kBM, w.lq, w.lk);
+    w.ntiles = max(w.nt[0], w.nt[1]);
+    w.has_b = w.row0 + kBM < w.lq;
+    return true;
+}
+
+// One row's share of a key tile: max over its 128 scores in tensor memory,
+// lazy update of the running max m (new max only when it grows by > 2^8),
+// then P = 2^(S*scale - m) written back as bf16 over the S columns.  MASK
+// selects the bottom-right causal / sequence-end masking; tiles that lie
+// inside the row's visible range take the mask-free instantiation.
+template <bool MASK, bool BF16>
+__device__ __forceinline__ void softmax_tile(uint32_t s_col, int kbase, int limit, float sl2, float& m, float& alpha,
+                                             bool& rescale, float& sum) {
+    float mx;
+    {
+        float v[kBN];
+#pragma unroll
+        for (int c = 0; c < kBN / 32; ++c) tc::tmem_ld32(s_col + c * 32, *reinterpret_cast<float(*)[32]>(&v[c * 32]));
+        tc::tmem_wait_ld();
+        float m8[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) m8[e] = -INFINITY;
+#pragma unroll
+        for (int e = 0; e < kBN; ++e) m8[e & 7] = fmaxf(m8[e & 7], (!MASK || kbase + e <= limit) ? v[e] : -INFINITY);
+        mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+    }
+    alpha = 1.f;
+    rescale = false;
+    if (mx != -INFINITY && (m == -INFINITY || (mx - m) * sl2 > kRescaleLog2)) {
+        alpha = m == -INFINITY ? 0.f : fast_exp2((m - mx) * sl2);
+        rescale = m != -INFINITY;
+        m = mx;
+    }
+    const float msl = m == -INFINITY ? 0.f : m * sl2;
+    float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+    for (int c2 = 0; c2 < kBN / 64; ++c2) {
+        float v[64];
+        tc::tmem_ld32(s_col + c2 * 64, *reinterpret_cast<float(*)[32]>(&v[0]));
+        tc::tmem_ld32(s_col + c2 * 64 + 32, *reinterpret_cast<float(*)[32]>(&v[32]));
+        tc::tmem_wait_ld();
+        uint32_t pk[32];
+#pragma unroll
+        for (int e = 0; e < 64; e += 2) {
+            float a = fast_exp2(fmaf(v[e], sl2, -msl));
+            float b = fast_exp2(fmaf(v[e + 1], sl2, -msl));
+            if (MASK) {
+                if (kbase + c2 * 64 + e > limit) a = 0.f;
+                if (kbase + c2 * 64 + e + 1 > limit) b = 0.f;
+            }
+            sum4[(e >> 1) & 3] += a + b;
+            pk[e / 2] = pack2<BF16>(a, b);
+        }
+        // P for 64 keys occupies 32 TMEM columns at s_col + 32*c2; S columns
+        // 64*c2 .. 64*c2+63 were already read, so the write never runs ahead.
+        tc::tmem_st32(s_col + c2 * 32, pk);
+    }
+    sum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
+}
+
 template <bool BF16>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtensorMap tmq,
@@ -82,33 +179,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     extern __shared__ uint8_t smem_raw[];
     Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-
-    const int h = blockIdx.x;
-    const int blk_q = p.q_blocks - 1 - int(blockIdx.y);  // longest (latest) rows first
-    const int s = blockIdx.z;
-    const int q0 = p.cu_q[s], lq = p.cu_q[s + 1] - q0;
-    const int k0 = p.cu_k[s], lk = p.cu_k[s + 1] - k0;
-    const int row0 = blk_q * 2 * kBM;
-    if (row0 >= lq) return;  // uniform across the CTA
-    const int nt[2] = {key_tiles(row0, row0 + kBM, lq, lk), key_tiles(row0 + kBM, row0 + 2 * kBM, lq, lk)};
-    const int ntiles = max(nt[0], nt[1]);
-    const bool has_b = row0 + kBM < lq;
-    const int kvh = h / p.group;
-
-    if (ntiles == 0) {  // no visible key for any row: zero output
-        const int rows = min(2 * kBM, lq - row0);
-        for (int i = tid; i < rows * (kD / 8); i += kThreads) {
-            const int r = row0 + i / (kD / 8), c = i % (kD / 8);
-            reinterpret_cast<uint4*>(p.out + int64_t(q0 + r) * p.out_stride + h * kD)[c] = make_uint4(0, 0, 0, 0);
-        }
-        return;
-    }
+    const int total_units = p.q_blocks * p.num_seqs * p.hq;
 
     if (tid == 0) {
         mbar_init(&sm.q_full, 1);
-        for (int i = 0; i < kStages; ++i) {
-            mbar_init(&sm.kv_full[i], 1);
-            mbar_init(&sm.kv_empty[i], 1);
+        mbar_init(&sm.q_empty, 1);
+        for (int i = 0; i < kKStages; ++i) {
+            mbar_init(&sm.k_full[i], 1);
+            mbar_init(&sm.k_empty[i], 1);
+        }
+        for (int i = 0; i < kVStages; ++i) {
+            mbar_init(&sm.v_full[i], 1);
+            mbar_init(&sm.v_empty[i], 1);
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&sm.s_full[i], 1);
@@ -127,51 +209,69 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc::fence_after_sync();
     const uint32_t tmem = sm.tmem_base;
+    auto failed = [&]() { return *reinterpret_cast<volatile int32_t*>(&sm.err) != 0; };
 
     if (warp == 0) {
         // ------------------------------------------------------------ producer
-        if (lane == 0) {
-            prefetch_tmap(&tmq);
-            prefetch_tmap(&tmk);
-            prefetch_tmap(&tmv);
+        // lane 0: Q and K tiles; lane 1: V tiles (independent rings).
+        if (lane < 2) {
+            const bool kq = lane == 0;
+            if (kq) {
+                prefetch_tmap(&tmq);
+                prefetch_tmap(&tmk);
+            } else {
+                prefetch_tmap(&tmv);
+            }
             const uint64_t pol_q = l2_policy_evict_first();
             const uint64_t pol_kv = l2_policy_evict_last();  // K/V tiles are re-read by the group's q heads
-            mbar_arrive_expect_tx(&sm.q_full, (has_b ? 4 : 2) * kHalf);
-            for (int t = 0; t < (has_b ? 2 : 1); ++t) {
-                tma_load_2d(sm.q[t][0], &tmq, h * kD, q0 + row0 + t * kBM, &sm.q_full, pol_q);
-                tma_load_2d(sm.q[t][1], &tmq, h * kD + 64, q0 + row0 + t * kBM, &sm.q_full, pol_q);
-            }
-            const int32_t* bt = p.block_tables ? p.block_tables + int64_t(s) * p.bt_stride : nullptr;
-            int filled = 0;
-            for (int j = 0; j < ntiles; ++j) {
-                const int st = j % kStages;
-                if (*reinterpret_cast<volatile int32_t*>(&sm.err) ||
-                    !wait_or_flag(&sm.kv_empty[st], ((j / kStages) & 1) ^ 1, sm))
-                    break;
-                int y;
-                if (bt) {
-                    const int pos = j * kBN;
-                    const int lb = pos / p.block_size;
-                    const int blk = lb < p.bt_stride ? bt[lb] : -1;
-                    y = (blk >= 0 && blk < p.num_blocks) ? blk * p.block_size + (pos - lb * p.block_size)
-                                                         : p.num_blocks * p.block_size;
-                } else {
-                    y = k0 + j * kBN;
+            const int NS = kq ? kKStages : kVStages;
+            uint64_t* full = kq ? sm.k_full : sm.v_full;
+            uint64_t* empty = kq ? sm.k_empty : sm.v_empty;
+            const CUtensorMap* tm = kq ? &tmk : &tmv;
+            int nq = 0, g = 0;  // units loaded, tiles loaded (across units)
+            Unit w;
+            for (int k = 0;; ++k) {
+                const int u = unit_at(k, blockIdx.x, gridDim.x);
+                if (u >= total_units || failed()) break;
+                if (!load_unit(p, u, w) || w.ntiles == 0) continue;
+                if (kq) {
+                    // Q of the previous unit must no longer be read by S MMAs.
+                    if (!wait_or_flag(&sm.q_empty, (nq & 1) ^ 1, sm)) break;
+                    mbar_arrive_expect_tx(&sm.q_full, (w.has_b ? 4 : 2) * kHalf);
+                    for (int t = 0; t < (w.has_b ? 2 : 1); ++t) {
+                        tma_load_2d(sm.q[t][0], &tmq, w.h * kD, w.q0 + w.row0 + t * kBM, &sm.q_full, pol_q);
+                        tma_load_2d(sm.q[t][1], &tmq, w.h * kD + 64, w.q0 + w.row0 + t * kBM, &sm.q_full, pol_q);
+                    }
+                    ++nq;
                 }
-                mbar_arrive_expect_tx(&sm.kv_full[st], 4 * kHalf);
-                const int x = kvh * kD;
-                tma_load_2d(sm.kv[st][0], &tmk, x, y, &sm.kv_full[st], pol_kv);
-                tma_load_2d(sm.kv[st][1], &tmk, x + 64, y, &sm.kv_full[st], pol_kv);
-                tma_load_2d(sm.kv[st][2], &tmv, x, y, &sm.kv_full[st], pol_kv);
-                tma_load_2d(sm.kv[st][3], &tmv, x + 64, y, &sm.kv_full[st], pol_kv);
-                ++filled;
+                const int32_t* bt = p.block_tables ? p.block_tables + int64_t(w.s) * p.bt_stride : nullptr;
+                const int x = (w.h / p.group) * kD;
+                for (int j = 0; j < w.ntiles; ++j, ++g) {
+                    const int st = g % NS;
+                    if (failed() || !wait_or_flag(&empty[st], ((g / NS) & 1) ^ 1, sm)) break;
+                    int y;
+                    if (bt) {
+                        const int pos = j * kBN;
+                        const int lb = pos / p.block_size;
+                        const int blk = lb < p.bt_stride ? bt[lb] : -1;
+                        y = (blk >= 0 && blk < p.num_blocks) ? blk * p.block_size + (pos - lb * p.block_size)
+                                                             : p.num_blocks * p.block_size;
+                    } else {
+                        y = w.k0 + j * kBN;
+                    }
+                    mbar_arrive_expect_tx(&full[st], 2 * kHalf);
+                    uint8_t* dst0 = kq ? sm.k[st][0] : sm.v[st][0];
+                    uint8_t* dst1 = kq ? sm.k[st][1] : sm.v[st][1];
+                    tma_load_2d(dst0, tm, x, y, &full[st], pol_kv);
+                    tma_load_2d(dst1, tm, x + 64, y, &full[st], pol_kv);
+                }
             }
             // Before the CTA exits, every load issued into its shared memory must have
             // landed (always true on the normal path; bounded wait on error paths).
-            mbar_wait(&sm.q_full, 0);
-            for (int st = 0; st < kStages && st < filled; ++st) {
-                const int last = st + ((filled - 1 - st) / kStages) * kStages;
-                mbar_wait(&sm.kv_full[st], (last / kStages) & 1);
+            if (kq && nq > 0) mbar_wait(&sm.q_full, (nq - 1) & 1);
+            for (int st = 0; st < NS && st < g; ++st) {
+                const int last = st + ((g - 1 - st) / NS) * NS;
+                mbar_wait(&full[st], (last / NS) & 1);
             }
         }
     } else if (warp == 1) {
@@ -179,11 +279,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             constexpr uint32_t idS = tc::idesc_f16<BF16>(kBM, kBN, false, false);
             constexpr uint32_t idPV = tc::idesc_f16<BF16>(kBM, kD, false, true);
-            bool ok = wait_or_flag(&sm.q_full, 0, sm);
-            tc::fence_after_sync();
-            auto issue_s = [&](int t, int j) {
+            int nq = 0, g = 0;
+            int npv[2] = {0, 0};  // P tiles consumed per query tile (across units)
+            bool ok = true;
+            auto issue_s = [&](int t, int kst) {
                 const uint32_t qa = smem_u32(sm.q[t][0]);
-                const uint32_t ka = smem_u32(sm.kv[j % kStages][0]);
+                const uint32_t ka = smem_u32(sm.k[kst][0]);
 #pragma unroll
                 for (int kk = 0; kk < kD / 16; ++kk) {
                     // K-major operands: 16 dims = 32 bytes inside a 128-byte swizzled row
@@ -193,41 +294,61 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 tc::commit(&sm.s_full[t]);
             };
-            auto issue_pv = [&](int t, int j) {
-                if (!wait_or_flag(&sm.p_ready[t], j & 1, sm)) return false;
+            auto issue_pv = [&](int t, int vst, bool first) {
+                if (!wait_or_flag(&sm.p_ready[t], npv[t] & 1, sm)) return false;
+                ++npv[t];
                 tc::fence_after_sync();
-                const uint32_t va = smem_u32(sm.kv[j % kStages][2]);
+                const uint32_t va = smem_u32(sm.v[vst][0]);
 #pragma unroll
                 for (int kk = 0; kk < kBN / 16; ++kk) {
                     // V is MN-major: 16 keys = two 8-row swizzle atoms (SBO 1024 B); the
                     // second 64 dims live in the V-hi half (LBO = kHalf).
                     tc::mma_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8,
                                tc::smem_desc_sw128(va + kk * 16 * 128, kHalf, 1024), idPV,
-                               (j > 0 || kk > 0) ? 1u : 0u);
+                               (!first || kk > 0) ? 1u : 0u);
                 }
                 tc::commit(&sm.o_done[t]);
                 return true;
             };
-            for (int j = 0; ok && j < ntiles; ++j) {
-                if (!wait_or_flag(&sm.kv_full[j % kStages], (j / kStages) & 1, sm)) { ok = false; break; }
+            // V tile of key tile g must have landed before its first PV.
+            auto wait_v = [&](int gg) { return wait_or_flag(&sm.v_full[gg % kVStages], (gg / kVStages) & 1, sm); };
+            Unit w;
+            for (int k = 0; ok; ++k) {
+                const int u = unit_at(k, blockIdx.x, gridDim.x);
+                if (u >= total_units || failed()) break;
+                if (!load_unit(p, u, w) || w.ntiles == 0) continue;
+                if (!wait_or_flag(&sm.q_full, nq & 1, sm)) { ok = false; break; }
+                ++nq;
                 tc::fence_after_sync();
-                // tile A: PV(j-1) frees S_A before S_A(j) overwrites it (in-order tensor pipe)
-                if (j < nt[0]) {
-                    if (j > 0 && !issue_pv(0, j - 1)) { ok = false; break; }
-                    issue_s(0, j);
-                } else if (j == nt[0] && j > 0) {
-                    if (!issue_pv(0, j - 1)) { ok = false; break; }
+                const int g0 = g;
+                for (int j = 0; j < w.ntiles; ++j) {
+                    const int gj = g0 + j, kst = gj % kKStages, pvs = (gj - 1) % kVStages;
+                    if (!wait_or_flag(&sm.k_full[kst], (gj / kKStages) & 1, sm)) { ok = false; break; }
+                    if (j > 0 && !wait_v(gj - 1)) { ok = false; break; }
+                    tc::fence_after_sync();
+                    // tile A: PV(j-1) frees S_A before S_A(j) overwrites it (in-order tensor pipe)
+                    if (j < w.nt[0]) {
+                        if (j > 0 && !issue_pv(0, pvs, j == 1)) { ok = false; break; }
+                        issue_s(0, kst);
+                    } else if (j == w.nt[0] && j > 0) {
+                        if (!issue_pv(0, pvs, j == 1)) { ok = false; break; }
+                    }
+                    if (j < w.nt[1]) {
+                        if (j > 0 && !issue_pv(1, pvs, j == 1)) { ok = false; break; }
+                        issue_s(1, kst);
+                    }
+                    tc::commit(&sm.k_empty[kst]);                  // both S of tile j issued
+                    if (j == w.ntiles - 1) tc::commit(&sm.q_empty);  // last S of the unit issued
+                    if (j > 0) tc::commit(&sm.v_empty[pvs]);       // both PVs of tile j-1 issued
                 }
-                if (j < nt[1]) {
-                    if (j > 0 && !issue_pv(1, j - 1)) { ok = false; break; }
-                    issue_s(1, j);
-                }
-                if (j > 0) tc::commit(&sm.kv_empty[(j - 1) % kStages]);  // both PVs of tile j-1 issued
-            }
-            if (ok) {
-                if (nt[0] == ntiles) ok = issue_pv(0, ntiles - 1);
-                if (ok && nt[1] == ntiles) ok = issue_pv(1, ntiles - 1);
-                tc::commit(&sm.kv_empty[(ntiles - 1) % kStages]);
+                if (!ok) break;
+                const int gl = g0 + w.ntiles - 1, lvs = gl % kVStages;
+                if (!wait_v(gl)) { ok = false; break; }
+                tc::fence_after_sync();
+                if (w.nt[0] == w.ntiles && !issue_pv(0, lvs, w.ntiles == 1)) { ok = false; break; }
+                if (w.nt[1] == w.ntiles && !issue_pv(1, lvs, w.ntiles == 1)) { ok = false; break; }
+                tc::commit(&sm.v_empty[lvs]);
+                g = g0 + w.ntiles;
             }
             // Wait (bounded) for every MMA issued above before the tensor memory is freed.
             tc::commit(&sm.drain);
@@ -241,118 +362,101 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t lane_addr = uint32_t(quarter * 32) << 16;
         const uint32_t s_col = tmem + lane_addr + t * 128;
         const uint32_t o_col = tmem + lane_addr + 256 + t * 128;
-        const int qrow = row0 + t * kBM + r;
-        const int limit = qrow < lq ? qrow + (lk - lq) : -1;  // last visible key of this row
         const float sl2 = p.scale_log2;
-        const int my_tiles = nt[t];
-        float m = -INFINITY, l = 0.f;
-        bool ok = true;
-        for (int j = 0; j < my_tiles; ++j) {
-            if (!wait_or_flag(&sm.s_full[t], j & 1, sm)) { ok = false; break; }
-            tc::fence_after_sync();
-            const int kbase = j * kBN;
-            const bool full_row = kbase + kBN - 1 <= limit;  // no masking needed in this tile
-            // pass 1: row max
-            float mx = -INFINITY;
-#pragma unroll 1
-            for (int c = 0; c < kBN / 32; ++c) {
-                float v[32];
-                tc::tmem_ld32(s_col + c * 32, v);
-                tc::tmem_wait_ld();
-                float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    const float x = (full_row || kbase + c * 32 + e <= limit) ? v[e] : -INFINITY;
-                    m4[e & 3] = fmaxf(m4[e & 3], x);
-                }
-                mx = fmaxf(mx, fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])));
+        int ns = 0;  // S tiles of this query tile consumed (across units) = PVs issued for it
+        int g = 0;   // K/V tiles streamed so far (across units), to find a tile's stage
+        Unit w;
+        for (int k = 0;; ++k) {
+            const int u = unit_at(k, blockIdx.x, gridDim.x);
+            if (u >= total_units || failed()) break;
+            if (!load_unit(p, u, w)) continue;
+            const int g0 = g;
+            g += w.ntiles;
+            const int qrow = w.row0 + t * kBM + r;
+            const int my_tiles = w.nt[t];
+            uint4* dst = reinterpret_cast<uint4*>(p.out + int64_t(w.q0 + qrow) * p.out_stride + w.h * kD);
+            if (my_tiles == 0) {  // rows that see no key at all (only when lk < lq)
+                if (qrow < w.lq)
+                    for (int c = 0; c < kD / 8; ++c) dst[c] = make_uint4(0, 0, 0, 0);
+                continue;
             }
-            // Lazy rescale: keep the old max unless the new one exceeds it by 2^8.
-            float alpha = 1.f;
-            bool rescale = false;
-            if (mx != -INFINITY && (m == -INFINITY || (mx - m) * sl2 > kRescaleLog2)) {
-                alpha = m == -INFINITY ? 0.f : fast_exp2((m - mx) * sl2);
-                rescale = m != -INFINITY;
-                m = mx;
-            }
-            const float msl = m == -INFINITY ? 0.f : m * sl2;
-            // pass 2: P = exp2(S*scale - m) as bf16 over the S columns, row sum
-            float sum4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 1
-            for (int c = 0; c < kBN / 32; ++c) {
-                float v[32];
-                tc::tmem_ld32(s_col + c * 32, v);
-                tc::tmem_wait_ld();
-                uint32_t pk[16];
-#pragma unroll
-                for (int e = 0; e < 32; e += 2) {
-                    const bool in0 = full_row || kbase + c * 32 + e <= limit;
-                    const bool in1 = full_row || kbase + c * 32 + e + 1 <= limit;
-                    const float a = in0 ? fast_exp2(fmaf(v[e], sl2, -msl)) : 0.f;
-                    const float b = in1 ? fast_exp2(fmaf(v[e + 1], sl2, -msl)) : 0.f;
-                    sum4[(e >> 1) & 3] += a + b;
-                    pk[e / 2] = pack2<BF16>(a, b);
-                }
-                // P chunk c (32 keys) occupies 16 TMEM columns at s_col + 16c
-                tc::tmem_st16(s_col + c * 16, pk);
-            }
-            l = fmaf(l, alpha, (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
-            if (rescale && j > 0) {
-                // O must hold PV(j-1) before it is scaled.
-                if (!wait_or_flag(&sm.o_done[t], (j - 1) & 1, sm)) { ok = false; break; }
+            const int limit = qrow < w.lq ? qrow + (w.lk - w.lq) : -1;  // last visible key of this row
+            const int ns0 = ns;
+            float m = -INFINITY, l = 0.f;
+            bool ok = true;
+            for (int j = 0; j < my_tiles; ++j) {
+                if (!wait_or_flag(&sm.s_full[t], ns & 1, sm)) { ok = false; break; }
+                ++ns;
                 tc::fence_after_sync();
+                const int kbase = j * kBN;
+                // Tiles inside the visible range of all 32 rows of this warp need no mask.
+                // tcgen05.ld/st are warp-collective, so the choice must be warp-uniform.
+                const bool full_row = __all_sync(0xffffffffu, kbase + kBN - 1 <= limit);
+                float alpha, sum;
+                bool rescale;
+                if (full_row)
+                    softmax_tile<false, BF16>(s_col, kbase, limit, sl2, m, alpha, rescale, sum);
+                else
+                    softmax_tile<true, BF16>(s_col, kbase, limit, sl2, m, alpha, rescale, sum);
+                l = fmaf(l, alpha, sum);
+                // Warp-collective O rescale when any row of the warp needs it (alpha = 1 elsewhere).
+                if (__any_sync(0xffffffffu, rescale && j > 0)) {
+                    if (!(rescale && j > 0)) alpha = 1.f;
+                    // O must hold PV(j-1) of this unit before it is scaled.
+                    if (!wait_or_flag(&sm.o_done[t], (ns0 + j - 1) & 1, sm)) { ok = false; break; }
+                    tc::fence_after_sync();
 #pragma unroll 1
-                for (int c = 0; c < kD / 32; ++c) {
-                    float o[32];
-                    tc::tmem_ld32(o_col + c * 32, o);
-                    tc::tmem_wait_ld();
-                    uint32_t u[32];
+                    for (int c = 0; c < kD / 32; ++c) {
+                        float o[32];
+                        tc::tmem_ld32(o_col + c * 32, o);
+                        tc::tmem_wait_ld();
+                        uint32_t uo[32];
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) u[e] = __float_as_uint(o[e] * alpha);
-                    tc::tmem_st32(o_col + c * 32, u);
+                        for (int e = 0; e < 32; ++e) uo[e] = __float_as_uint(o[e] * alpha);
+                        tc::tmem_st32(o_col + c * 32, uo);
+                    }
                 }
-            }
-            tc::tmem_wait_st();
-            // Cache rows past this sequence's keys may hold NaN bits; P is 0 there but
-            // 0 * NaN is NaN, so the first tile to use the stage clears those V rows.
-            if (kbase + kBN > lk && (t == 0 || j >= nt[0])) {
-                if (kbase + r >= lk) {
-                    uint4* v0 = reinterpret_cast<uint4*>(sm.kv[j % kStages][2] + r * 128);
-                    uint4* v1 = reinterpret_cast<uint4*>(sm.kv[j % kStages][3] + r * 128);
+                tc::tmem_wait_st();
+                // Cache rows past this sequence's keys may hold NaN bits; P is 0 there but
+                // 0 * NaN is NaN, so the first tile to use the stage clears those V rows.
+                if (kbase + kBN > w.lk && (t == 0 || j >= w.nt[0])) {
+                    const int gj = g0 + j, st = gj % kVStages;
+                    if (!wait_or_flag(&sm.v_full[st], (gj / kVStages) & 1, sm)) { ok = false; break; }
+                    if (kbase + r >= w.lk) {
+                        uint4* v0 = reinterpret_cast<uint4*>(sm.v[st][0] + r * 128);
+                        uint4* v1 = reinterpret_cast<uint4*>(sm.v[st][1] + r * 128);
 #pragma unroll
-                    for (int c = 0; c < 8; ++c) v0[c] = v1[c] = make_uint4(0, 0, 0, 0);
+                        for (int c = 0; c < 8; ++c) v0[c] = v1[c] = make_uint4(0, 0, 0, 0);
+                    }
+                    fence_proxy_async_smem();
                 }
-                fence_proxy_async_smem();
+                tc::fence_before_sync();
+                mbar_arrive(&sm.p_ready[t]);
             }
-            tc::fence_before_sync();
-            mbar_arrive(&sm.p_ready[t]);
-        }
-        // ---- epilogue: O / l -> bf16, one query row per thread ----
-        if (ok && my_tiles > 0 && wait_or_flag(&sm.o_done[t], (my_tiles - 1) & 1, sm)) {
+            if (!ok) break;
+            // ---- epilogue: O / l -> bf16, one query row per thread.  Loading O before
+            // this warpgroup's next p_ready arrive orders it before the next unit's
+            // first PV overwrites O.
+            if (!wait_or_flag(&sm.o_done[t], (ns - 1) & 1, sm)) break;
             tc::fence_after_sync();
             const float inv = l > 0.f ? 1.f / l : 0.f;
-            uint4* dst = reinterpret_cast<uint4*>(p.out + int64_t(q0 + qrow) * p.out_stride + h * kD);
 #pragma unroll 1
             for (int c = 0; c < kD / 32; ++c) {
                 float o[32];
                 tc::tmem_ld32(o_col + c * 32, o);
                 tc::tmem_wait_ld();
-                if (qrow < lq) {
+                if (qrow < w.lq) {
 #pragma unroll
                     for (int e = 0; e < 32; e += 8) {
-                        uint4 w;
-                        w.x = pack2<BF16>(o[e] * inv, o[e + 1] * inv);
-                        w.y = pack2<BF16>(o[e + 2] * inv, o[e + 3] * inv);
-                        w.z = pack2<BF16>(o[e + 4] * inv, o[e + 5] * inv);
-                        w.w = pack2<BF16>(o[e + 6] * inv, o[e + 7] * inv);
-                        dst[(c * 32 + e) / 8] = w;
+                        uint4 v4;
+                        v4.x = pack2<BF16>(o[e] * inv, o[e + 1] * inv);
+                        v4.y = pack2<BF16>(o[e + 2] * inv, o[e + 3] * inv);
+                        v4.z = pack2<BF16>(o[e + 4] * inv, o[e + 5] * inv);
+                        v4.w = pack2<BF16>(o[e + 6] * inv, o[e + 7] * inv);
+                        dst[(c * 32 + e) / 8] = v4;
                     }
                 }
             }
-        } else if (my_tiles == 0 && qrow < lq) {
-            // rows of tile B that see no key (possible only when lk < lq)
-            uint4* dst = reinterpret_cast<uint4*>(p.out + int64_t(q0 + qrow) * p.out_stride + h * kD);
-            for (int c = 0; c < kD / 8; ++c) dst[c] = make_uint4(0, 0, 0, 0);
         }
     }
 
@@ -399,8 +503,9 @@ extern "C" int32_t b200_varlen_prefill(void* out, const void* q, int64_t q_strid
         B200_REQUIRE(total_k_rows % block_size == 0, "varlen_prefill: cache rows %d not whole blocks", total_k_rows);
     }
     const int q_blocks = (max_seqlen_q + 2 * kBM - 1) / (2 * kBM);
-    if (q_blocks > 65535 || num_seqs > 65535)
-        return fail(B200_ERR_UNSUPPORTED, "varlen_prefill: %d query blocks x %d sequences", q_blocks, num_seqs);
+    if (int64_t(q_blocks) * num_seqs * num_heads > INT32_MAX / 2)
+        return fail(B200_ERR_UNSUPPORTED, "varlen_prefill: %d query blocks x %d sequences x %d heads", q_blocks,
+                    num_seqs, num_heads);
     const bool bf16 = dtype == B200_BF16;
     // The tensor maps span exactly the caller's q / k / v rows, so a tile that
     // runs past the last token reads the TMA fill value (zero), never memory
@@ -436,7 +541,8 @@ extern "C" int32_t b200_varlen_prefill(void* out, const void* q, int64_t q_strid
     const int smem = int(sizeof(Smem)) + 1024;
     const void* fn = bf16 ? (const void*)prefill_kernel<true> : (const void*)prefill_kernel<false>;
     ensure_smem_attr(fn, smem);
-    const dim3 grid(num_heads, q_blocks, num_seqs);
+    const int64_t units = int64_t(q_blocks) * num_seqs * num_heads;
+    const dim3 grid(unsigned(units < device_sm_count() ? units : device_sm_count()));
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (bf16) prefill_kernel<true><<<grid, kThreads, smem, st>>>(prm, tmq, tmk, tmv);
     else prefill_kernel<false><<<grid, kThreads, smem, st>>>(prm, tmq, tmk, tmv);
