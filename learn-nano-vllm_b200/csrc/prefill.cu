@@ -125,19 +125,23 @@ __device__ __forceinline__ bool load_unit(const Params& p, int u, Unit& w) {
 template <bool MASK, bool BF16>
 __device__ __forceinline__ void softmax_tile(uint32_t s_col, int kbase, int limit, float sl2, float& m, float& alpha,
                                              bool& rescale, float& sum) {
-    float mx;
-    {
-        float v[kBN];
+    // One round trip to tensor memory: all 128 scores of the row in registers.
+    float v[kBN];
 #pragma unroll
-        for (int c = 0; c < kBN / 32; ++c) tc::tmem_ld32(s_col + c * 32, *reinterpret_cast<float(*)[32]>(&v[c * 32]));
-        tc::tmem_wait_ld();
-        float m8[8];
+    for (int c = 0; c < kBN / 32; ++c) tc::tmem_ld32(s_col + c * 32, *reinterpret_cast<float(*)[32]>(&v[c * 32]));
+    tc::tmem_wait_ld();
+    if (MASK) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) m8[e] = -INFINITY;
-#pragma unroll
-        for (int e = 0; e < kBN; ++e) m8[e & 7] = fmaxf(m8[e & 7], (!MASK || kbase + e <= limit) ? v[e] : -INFINITY);
-        mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+        for (int e = 0; e < kBN; ++e)
+            if (kbase + e > limit) v[e] = -INFINITY;
     }
+    float m8[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) m8[e] = v[e];
+#pragma unroll
+    for (int e = 8; e < kBN; ++e) m8[e & 7] = fmaxf(m8[e & 7], v[e]);
+    const float mx =
+        fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
     alpha = 1.f;
     rescale = false;
     if (mx != -INFINITY && (m == -INFINITY || (mx - m) * sl2 > kRescaleLog2)) {
@@ -147,26 +151,18 @@ __device__ __forceinline__ void softmax_tile(uint32_t s_col, int kbase, int limi
     }
     const float msl = m == -INFINITY ? 0.f : m * sl2;
     float sum4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 1
+#pragma unroll
     for (int c2 = 0; c2 < kBN / 64; ++c2) {
-        float v[64];
-        tc::tmem_ld32(s_col + c2 * 64, *reinterpret_cast<float(*)[32]>(&v[0]));
-        tc::tmem_ld32(s_col + c2 * 64 + 32, *reinterpret_cast<float(*)[32]>(&v[32]));
-        tc::tmem_wait_ld();
         uint32_t pk[32];
 #pragma unroll
         for (int e = 0; e < 64; e += 2) {
-            float a = fast_exp2(fmaf(v[e], sl2, -msl));
-            float b = fast_exp2(fmaf(v[e + 1], sl2, -msl));
-            if (MASK) {
-                if (kbase + c2 * 64 + e > limit) a = 0.f;
-                if (kbase + c2 * 64 + e + 1 > limit) b = 0.f;
-            }
+            // masked scores are -inf, and ex2 of -inf is +0
+            const float a = fast_exp2(fmaf(v[c2 * 64 + e], sl2, -msl));
+            const float b = fast_exp2(fmaf(v[c2 * 64 + e + 1], sl2, -msl));
             sum4[(e >> 1) & 3] += a + b;
             pk[e / 2] = pack2<BF16>(a, b);
         }
-        // P for 64 keys occupies 32 TMEM columns at s_col + 32*c2; S columns
-        // 64*c2 .. 64*c2+63 were already read, so the write never runs ahead.
+        // P for 64 keys occupies 32 TMEM columns at s_col + 32*c2 (over S, already read)
         tc::tmem_st32(s_col + c2 * 32, pk);
     }
     sum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
