@@ -225,6 +225,17 @@ __device__ __forceinline__ uint16_t to_bits16(float x) {
     }
 }
 
+// Per-thread register budget of the calling warpgroup (all four warps execute
+// the same call); .inc takes registers released by .dec of other warpgroups.
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 __device__ __forceinline__ void named_bar_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }

@@ -39,7 +39,17 @@ constexpr int kD = 128;
 constexpr int kHalf = kBM * 128;  // one 64-dim half of a 128-row tile: 16 KiB
 constexpr int kKStages = 3;  // K tiles are released after S, so they can run further ahead
 constexpr int kVStages = 2;  // V tiles are released after PV
-constexpr int kThreads = 320;
+// Warpgroups: 0 = softmax of tile A, 1 = softmax of tile B, 2 = control
+// (warp 8 producer, warp 9 MMA issuer, warps 10-11 idle).  setmaxnreg moves
+// registers from the control warpgroup to the softmax warpgroups; the split
+// must fit the block's launch allocation: 2*128*kRegsSoftmax + 128*kRegsControl
+// <= kThreads * 168.
+constexpr int kThreads = 384;
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr uint32_t kRegsSoftmax = 216;
+constexpr uint32_t kRegsControl = 64;
+static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsControl <= kThreads * 168, "register split exceeds the launch allocation");
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleLog2 = 8.0f;
 
@@ -197,7 +207,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         sm.err = 0;
         fence_mbar_init();
     }
-    if (warp == 1) {
+    if (warp == kMmaWarp) {
         tc::tmem_alloc(&sm.tmem_base, kTmemCols);
         tc::tmem_relinquish();
     }
@@ -207,152 +217,158 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem = sm.tmem_base;
     auto failed = [&]() { return *reinterpret_cast<volatile int32_t*>(&sm.err) != 0; };
 
-    if (warp == 0) {
-        // ------------------------------------------------------------ producer
-        // lane 0: Q and K tiles; lane 1: V tiles (independent rings).
-        if (lane < 2) {
-            const bool kq = lane == 0;
-            if (kq) {
-                prefetch_tmap(&tmq);
-                prefetch_tmap(&tmk);
-            } else {
-                prefetch_tmap(&tmv);
-            }
-            const uint64_t pol_q = l2_policy_evict_first();
-            const uint64_t pol_kv = l2_policy_evict_last();  // K/V tiles are re-read by the group's q heads
-            const int NS = kq ? kKStages : kVStages;
-            uint64_t* full = kq ? sm.k_full : sm.v_full;
-            uint64_t* empty = kq ? sm.k_empty : sm.v_empty;
-            const CUtensorMap* tm = kq ? &tmk : &tmv;
-            int nq = 0, g = 0;  // units loaded, tiles loaded (across units)
-            Unit w;
-            for (int k = 0;; ++k) {
-                const int u = unit_at(k, blockIdx.x, gridDim.x);
-                if (u >= total_units || failed()) break;
-                if (!load_unit(p, u, w) || w.ntiles == 0) continue;
+    // setmaxnreg sits at the top of each warpgroup's branch, so that no code
+    // after it is shared between warpgroups of different register budgets.
+    if (warp >= 8) {
+        setmaxnreg_dec<kRegsControl>();
+        if (warp == kProducerWarp) {
+            // ------------------------------------------------------------ producer
+            // lane 0: Q and K tiles; lane 1: V tiles (independent rings).
+            if (lane < 2) {
+                const bool kq = lane == 0;
                 if (kq) {
-                    // Q of the previous unit must no longer be read by S MMAs.
-                    if (!wait_or_flag(&sm.q_empty, (nq & 1) ^ 1, sm)) break;
-                    mbar_arrive_expect_tx(&sm.q_full, (w.has_b ? 4 : 2) * kHalf);
-                    for (int t = 0; t < (w.has_b ? 2 : 1); ++t) {
-                        tma_load_2d(sm.q[t][0], &tmq, w.h * kD, w.q0 + w.row0 + t * kBM, &sm.q_full, pol_q);
-                        tma_load_2d(sm.q[t][1], &tmq, w.h * kD + 64, w.q0 + w.row0 + t * kBM, &sm.q_full, pol_q);
-                    }
-                    ++nq;
+                    prefetch_tmap(&tmq);
+                    prefetch_tmap(&tmk);
+                } else {
+                    prefetch_tmap(&tmv);
                 }
-                const int32_t* bt = p.block_tables ? p.block_tables + int64_t(w.s) * p.bt_stride : nullptr;
-                const int x = (w.h / p.group) * kD;
-                for (int j = 0; j < w.ntiles; ++j, ++g) {
-                    const int st = g % NS;
-                    if (failed() || !wait_or_flag(&empty[st], ((g / NS) & 1) ^ 1, sm)) break;
-                    int y;
-                    if (bt) {
-                        const int pos = j * kBN;
-                        const int lb = pos / p.block_size;
-                        const int blk = lb < p.bt_stride ? bt[lb] : -1;
-                        y = (blk >= 0 && blk < p.num_blocks) ? blk * p.block_size + (pos - lb * p.block_size)
-                                                             : p.num_blocks * p.block_size;
-                    } else {
-                        y = w.k0 + j * kBN;
+                const uint64_t pol_q = l2_policy_evict_first();
+                const uint64_t pol_kv = l2_policy_evict_last();  // K/V tiles are re-read by the group's q heads
+                const int NS = kq ? kKStages : kVStages;
+                uint64_t* full = kq ? sm.k_full : sm.v_full;
+                uint64_t* empty = kq ? sm.k_empty : sm.v_empty;
+                const CUtensorMap* tm = kq ? &tmk : &tmv;
+                int nq = 0, g = 0;  // units loaded, tiles loaded (across units)
+                Unit w;
+                for (int k = 0;; ++k) {
+                    const int u = unit_at(k, blockIdx.x, gridDim.x);
+                    if (u >= total_units || failed()) break;
+                    if (!load_unit(p, u, w) || w.ntiles == 0) continue;
+                    if (kq) {
+                        // Q of the previous unit must no longer be read by S MMAs.
+                        if (!wait_or_flag(&sm.q_empty, (nq & 1) ^ 1, sm)) break;
+                        mbar_arrive_expect_tx(&sm.q_full, (w.has_b ? 4 : 2) * kHalf);
+                        for (int t = 0; t < (w.has_b ? 2 : 1); ++t) {
+                            tma_load_2d(sm.q[t][0], &tmq, w.h * kD, w.q0 + w.row0 + t * kBM, &sm.q_full, pol_q);
+                            tma_load_2d(sm.q[t][1], &tmq, w.h * kD + 64, w.q0 + w.row0 + t * kBM, &sm.q_full, pol_q);
+                        }
+                        ++nq;
                     }
-                    mbar_arrive_expect_tx(&full[st], 2 * kHalf);
-                    uint8_t* dst0 = kq ? sm.k[st][0] : sm.v[st][0];
-                    uint8_t* dst1 = kq ? sm.k[st][1] : sm.v[st][1];
-                    tma_load_2d(dst0, tm, x, y, &full[st], pol_kv);
-                    tma_load_2d(dst1, tm, x + 64, y, &full[st], pol_kv);
+                    const int32_t* bt = p.block_tables ? p.block_tables + int64_t(w.s) * p.bt_stride : nullptr;
+                    const int x = (w.h / p.group) * kD;
+                    for (int j = 0; j < w.ntiles; ++j, ++g) {
+                        const int st = g % NS;
+                        if (failed() || !wait_or_flag(&empty[st], ((g / NS) & 1) ^ 1, sm)) break;
+                        int y;
+                        if (bt) {
+                            const int pos = j * kBN;
+                            const int lb = pos / p.block_size;
+                            const int blk = lb < p.bt_stride ? bt[lb] : -1;
+                            y = (blk >= 0 && blk < p.num_blocks) ? blk * p.block_size + (pos - lb * p.block_size)
+                                                                 : p.num_blocks * p.block_size;
+                        } else {
+                            y = w.k0 + j * kBN;
+                        }
+                        mbar_arrive_expect_tx(&full[st], 2 * kHalf);
+                        uint8_t* dst0 = kq ? sm.k[st][0] : sm.v[st][0];
+                        uint8_t* dst1 = kq ? sm.k[st][1] : sm.v[st][1];
+                        tma_load_2d(dst0, tm, x, y, &full[st], pol_kv);
+                        tma_load_2d(dst1, tm, x + 64, y, &full[st], pol_kv);
+                    }
+                }
+                // Before the CTA exits, every load issued into its shared memory must have
+                // landed (always true on the normal path; bounded wait on error paths).
+                if (kq && nq > 0) mbar_wait(&sm.q_full, (nq - 1) & 1);
+                for (int st = 0; st < NS && st < g; ++st) {
+                    const int last = st + ((g - 1 - st) / NS) * NS;
+                    mbar_wait(&full[st], (last / NS) & 1);
                 }
             }
-            // Before the CTA exits, every load issued into its shared memory must have
-            // landed (always true on the normal path; bounded wait on error paths).
-            if (kq && nq > 0) mbar_wait(&sm.q_full, (nq - 1) & 1);
-            for (int st = 0; st < NS && st < g; ++st) {
-                const int last = st + ((g - 1 - st) / NS) * NS;
-                mbar_wait(&full[st], (last / NS) & 1);
-            }
-        }
-    } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            constexpr uint32_t idS = tc::idesc_f16<BF16>(kBM, kBN, false, false);
-            constexpr uint32_t idPV = tc::idesc_f16<BF16>(kBM, kD, false, true);
-            int nq = 0, g = 0;
-            int npv[2] = {0, 0};  // P tiles consumed per query tile (across units)
-            bool ok = true;
-            auto issue_s = [&](int t, int kst) {
-                const uint32_t qa = smem_u32(sm.q[t][0]);
-                const uint32_t ka = smem_u32(sm.k[kst][0]);
-#pragma unroll
-                for (int kk = 0; kk < kD / 16; ++kk) {
-                    // K-major operands: 16 dims = 32 bytes inside a 128-byte swizzled row
-                    const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
-                    tc::mma_ss(tmem + t * 128, tc::smem_desc_sw128(qa + off, 16, 1024),
-                               tc::smem_desc_sw128(ka + off, 16, 1024), idS, kk > 0 ? 1u : 0u);
-                }
-                tc::commit(&sm.s_full[t]);
-            };
-            auto issue_pv = [&](int t, int vst, bool first) {
-                if (!wait_or_flag(&sm.p_ready[t], npv[t] & 1, sm)) return false;
-                ++npv[t];
-                tc::fence_after_sync();
-                const uint32_t va = smem_u32(sm.v[vst][0]);
-#pragma unroll
-                for (int kk = 0; kk < kBN / 16; ++kk) {
-                    // V is MN-major: 16 keys = two 8-row swizzle atoms (SBO 1024 B); the
-                    // second 64 dims live in the V-hi half (LBO = kHalf).
-                    tc::mma_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8,
-                               tc::smem_desc_sw128(va + kk * 16 * 128, kHalf, 1024), idPV,
-                               (!first || kk > 0) ? 1u : 0u);
-                }
-                tc::commit(&sm.o_done[t]);
-                return true;
-            };
-            // V tile of key tile g must have landed before its first PV.
-            auto wait_v = [&](int gg) { return wait_or_flag(&sm.v_full[gg % kVStages], (gg / kVStages) & 1, sm); };
-            Unit w;
-            for (int k = 0; ok; ++k) {
-                const int u = unit_at(k, blockIdx.x, gridDim.x);
-                if (u >= total_units || failed()) break;
-                if (!load_unit(p, u, w) || w.ntiles == 0) continue;
-                if (!wait_or_flag(&sm.q_full, nq & 1, sm)) { ok = false; break; }
-                ++nq;
-                tc::fence_after_sync();
-                const int g0 = g;
-                for (int j = 0; j < w.ntiles; ++j) {
-                    const int gj = g0 + j, kst = gj % kKStages, pvs = (gj - 1) % kVStages;
-                    if (!wait_or_flag(&sm.k_full[kst], (gj / kKStages) & 1, sm)) { ok = false; break; }
-                    if (j > 0 && !wait_v(gj - 1)) { ok = false; break; }
+        } else if (warp == kMmaWarp) {
+            // ------------------------------------------------------------ MMA issuer
+            if (lane == 0) {
+                constexpr uint32_t idS = tc::idesc_f16<BF16>(kBM, kBN, false, false);
+                constexpr uint32_t idPV = tc::idesc_f16<BF16>(kBM, kD, false, true);
+                int nq = 0, g = 0;
+                int npv[2] = {0, 0};  // P tiles consumed per query tile (across units)
+                bool ok = true;
+                auto issue_s = [&](int t, int kst) {
+                    const uint32_t qa = smem_u32(sm.q[t][0]);
+                    const uint32_t ka = smem_u32(sm.k[kst][0]);
+    #pragma unroll
+                    for (int kk = 0; kk < kD / 16; ++kk) {
+                        // K-major operands: 16 dims = 32 bytes inside a 128-byte swizzled row
+                        const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
+                        tc::mma_ss(tmem + t * 128, tc::smem_desc_sw128(qa + off, 16, 1024),
+                                   tc::smem_desc_sw128(ka + off, 16, 1024), idS, kk > 0 ? 1u : 0u);
+                    }
+                    tc::commit(&sm.s_full[t]);
+                };
+                auto issue_pv = [&](int t, int vst, bool first) {
+                    if (!wait_or_flag(&sm.p_ready[t], npv[t] & 1, sm)) return false;
+                    ++npv[t];
                     tc::fence_after_sync();
-                    // tile A: PV(j-1) frees S_A before S_A(j) overwrites it (in-order tensor pipe)
-                    if (j < w.nt[0]) {
-                        if (j > 0 && !issue_pv(0, pvs, j == 1)) { ok = false; break; }
-                        issue_s(0, kst);
-                    } else if (j == w.nt[0] && j > 0) {
-                        if (!issue_pv(0, pvs, j == 1)) { ok = false; break; }
+                    const uint32_t va = smem_u32(sm.v[vst][0]);
+    #pragma unroll
+                    for (int kk = 0; kk < kBN / 16; ++kk) {
+                        // V is MN-major: 16 keys = two 8-row swizzle atoms (SBO 1024 B); the
+                        // second 64 dims live in the V-hi half (LBO = kHalf).
+                        tc::mma_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8,
+                                   tc::smem_desc_sw128(va + kk * 16 * 128, kHalf, 1024), idPV,
+                                   (!first || kk > 0) ? 1u : 0u);
                     }
-                    if (j < w.nt[1]) {
-                        if (j > 0 && !issue_pv(1, pvs, j == 1)) { ok = false; break; }
-                        issue_s(1, kst);
+                    tc::commit(&sm.o_done[t]);
+                    return true;
+                };
+                // V tile of key tile g must have landed before its first PV.
+                auto wait_v = [&](int gg) { return wait_or_flag(&sm.v_full[gg % kVStages], (gg / kVStages) & 1, sm); };
+                Unit w;
+                for (int k = 0; ok; ++k) {
+                    const int u = unit_at(k, blockIdx.x, gridDim.x);
+                    if (u >= total_units || failed()) break;
+                    if (!load_unit(p, u, w) || w.ntiles == 0) continue;
+                    if (!wait_or_flag(&sm.q_full, nq & 1, sm)) { ok = false; break; }
+                    ++nq;
+                    tc::fence_after_sync();
+                    const int g0 = g;
+                    for (int j = 0; j < w.ntiles; ++j) {
+                        const int gj = g0 + j, kst = gj % kKStages, pvs = (gj - 1) % kVStages;
+                        if (!wait_or_flag(&sm.k_full[kst], (gj / kKStages) & 1, sm)) { ok = false; break; }
+                        if (j > 0 && !wait_v(gj - 1)) { ok = false; break; }
+                        tc::fence_after_sync();
+                        // tile A: PV(j-1) frees S_A before S_A(j) overwrites it (in-order tensor pipe)
+                        if (j < w.nt[0]) {
+                            if (j > 0 && !issue_pv(0, pvs, j == 1)) { ok = false; break; }
+                            issue_s(0, kst);
+                        } else if (j == w.nt[0] && j > 0) {
+                            if (!issue_pv(0, pvs, j == 1)) { ok = false; break; }
+                        }
+                        if (j < w.nt[1]) {
+                            if (j > 0 && !issue_pv(1, pvs, j == 1)) { ok = false; break; }
+                            issue_s(1, kst);
+                        }
+                        tc::commit(&sm.k_empty[kst]);                  // both S of tile j issued
+                        if (j == w.ntiles - 1) tc::commit(&sm.q_empty);  // last S of the unit issued
+                        if (j > 0) tc::commit(&sm.v_empty[pvs]);       // both PVs of tile j-1 issued
                     }
-                    tc::commit(&sm.k_empty[kst]);                  // both S of tile j issued
-                    if (j == w.ntiles - 1) tc::commit(&sm.q_empty);  // last S of the unit issued
-                    if (j > 0) tc::commit(&sm.v_empty[pvs]);       // both PVs of tile j-1 issued
+                    if (!ok) break;
+                    const int gl = g0 + w.ntiles - 1, lvs = gl % kVStages;
+                    if (!wait_v(gl)) { ok = false; break; }
+                    tc::fence_after_sync();
+                    if (w.nt[0] == w.ntiles && !issue_pv(0, lvs, w.ntiles == 1)) { ok = false; break; }
+                    if (w.nt[1] == w.ntiles && !issue_pv(1, lvs, w.ntiles == 1)) { ok = false; break; }
+                    tc::commit(&sm.v_empty[lvs]);
+                    g = g0 + w.ntiles;
                 }
-                if (!ok) break;
-                const int gl = g0 + w.ntiles - 1, lvs = gl % kVStages;
-                if (!wait_v(gl)) { ok = false; break; }
-                tc::fence_after_sync();
-                if (w.nt[0] == w.ntiles && !issue_pv(0, lvs, w.ntiles == 1)) { ok = false; break; }
-                if (w.nt[1] == w.ntiles && !issue_pv(1, lvs, w.ntiles == 1)) { ok = false; break; }
-                tc::commit(&sm.v_empty[lvs]);
-                g = g0 + w.ntiles;
+                // Wait (bounded) for every MMA issued above before the tensor memory is freed.
+                tc::commit(&sm.drain);
+                mbar_wait(&sm.drain, 0);
             }
-            // Wait (bounded) for every MMA issued above before the tensor memory is freed.
-            tc::commit(&sm.drain);
-            mbar_wait(&sm.drain, 0);
         }
     } else {
+        setmaxnreg_inc<kRegsSoftmax>();
         // ------------------------------------------------------------ softmax / epilogue
-        const int t = warp >= 6 ? 1 : 0;  // query tile of this warpgroup
+        const int t = warp >> 2;          // query tile of this warpgroup
         const int quarter = warp & 3;     // TMEM lanes 32*quarter .. +31 belong to this warp
         const int r = quarter * 32 + lane;
         const uint32_t lane_addr = uint32_t(quarter * 32) << 16;
@@ -458,7 +474,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     tc::fence_before_sync();
     __syncthreads();
-    if (warp == 1) {
+    if (warp == kMmaWarp) {
         tc::fence_after_sync();
         tc::tmem_dealloc(tmem, kTmemCols);
     }
