@@ -3,28 +3,29 @@
 // nanovllm/layers/attention.py:64-70, with or without a block table (prefix
 // caching / chunked prefill reads keys from the paged cache).
 //
-// Persistent CTAs (one per SM) walk work units -- two 128-query tiles (A =
-// rows 0-127, B = rows 128-255 of a 256-row block) of one query head of one
-// sequence -- heaviest first; both tiles share every K/V tile.  Tensor memory
-// is allocated once; the K/V ring and every barrier phase run on across
-// units, the next unit's Q loads as soon as the last S MMA of the current one
-// completes, and its MMAs overlap the current unit's epilogue.  Warp roles:
-//   warp 0    producer: TMA loads (no multicast) of both Q tiles once and of
-//             128-key K and V tiles into a 2-stage ring (64 KiB per stage),
-//             all as 64-dim x 128-row boxes with 128-byte swizzle;
-//   warp 1    MMA issuer (one thread) and tensor-memory owner;
-//   warps 2-5 softmax of tile A, warps 6-9 softmax of tile B: one thread per
-//             query row (TMEM lane = row).
-// Tensor memory: S_A cols 0-127, S_B 128-255, O_A 256-383, O_B 384-511.  The
-// MMA order per key tile j is PV_A(j-1) S_A(j) PV_B(j-1) S_B(j) (ping-pong):
-// while one warpgroup turns S(j) into P(j), the tensor core works on the
-// other tile.  S = Q K^T is an SS MMA (M = N = 128, K-major operands); the
-// softmax writes P as bf16 over its S columns and O += P V reads P from
-// tensor memory (TS MMA) with V as an MN-major operand.  The softmax is two
-// passes over its TMEM row (max, then exp / pack / store by 32-column chunk)
-// and rescales its O row in tensor memory only when the running max grew by
-// more than 2^8 (lazy rescaling; the sum uses the same stale max, so the
-// result is exact).
+// Persistent CTAs (one per SM) walk work units -- two 128-query tiles A and B
+// that read the same K/V tiles: the same rows of two query heads of one kv
+// head when the GQA group is even, else rows r and r + 128 of one head --
+// heaviest first.  Tensor memory is allocated once; the K/V rings and every
+// barrier phase run on across units.  Warp roles (three warpgroups):
+//   warps 0-3 / 4-7  softmax of tile A / B, one thread per query row (TMEM
+//             lane = row), and the epilogue O / l -> out;
+//   warp 8    producer: TMA loads (no multicast) of both Q tiles and of
+//             128-key K tiles (3-stage ring) and V tiles (2-stage ring), all
+//             64-dim x 128-row boxes with 128-byte swizzle; lane 0 Q and K,
+//             lane 1 V;
+//   warp 9    S issuer (one thread): S = Q K^T, SS MMA, M = N = 128;
+//   warp 10   PV issuer (one thread): O += P V, TS MMA with P from tensor
+//             memory and V as an MN-major operand.
+// Tensor memory: one S buffer (cols 0-127) shared by both tiles, P_A / P_B
+// (bf16 pairs, cols 128-191 / 192-255), O_A / O_B (cols 256-383 / 384-511).
+// A softmax warpgroup loads its 128 scores per row into registers and frees
+// the S buffer at once, so the S MMA of the other tile runs while it computes
+// P; it then waits for its previous PV (P and O free), rescales O when the
+// running max grew by more than 2^8 (lazy rescaling: the sum uses the same
+// stale max, so the result is exact), and writes P.  The S and PV streams
+// share no tensor memory, so the two issuers never wait on each other, and
+// two issuing threads keep the tensor pipe busy where one cannot.
 #include <climits>
 
 #include "common.cuh"
@@ -40,7 +41,7 @@ constexpr int kHalf = kBM * 128;  // one 64-dim half of a 128-row tile: 16 KiB
 constexpr int kKStages = 3;  // K tiles are released after S, so they can run further ahead
 constexpr int kVStages = 2;  // V tiles are released after PV
 // Warpgroups: 0 = softmax of tile A, 1 = softmax of tile B, 2 = control
-// (warp 8 producer, warp 9 MMA issuer, warps 10-11 idle).  setmaxnreg moves
+// (warp 8 producer, warp 9 S issuer, warp 10 PV issuer, warp 11 idle).  setmaxnreg moves
 // registers from the control warpgroup to the softmax warpgroups; the split
 // must fit the block's launch allocation: 2*128*kRegsSoftmax + 128*kRegsControl
 // <= kThreads * 168.
@@ -51,6 +52,11 @@ constexpr uint32_t kRegsSoftmax = 216;
 constexpr uint32_t kRegsControl = 64;
 static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsControl <= kThreads * 168, "register split exceeds the launch allocation");
 constexpr uint32_t kTmemCols = 512;
+// Tensor memory columns: one S buffer shared by both tiles (f32, 128 keys),
+// P of tile t (bf16 pairs, 64 columns) and O of tile t (f32, 128 dims).
+constexpr uint32_t kColS = 0;
+constexpr uint32_t kColP = 128;  // + 64 * t
+constexpr uint32_t kColO = 256;  // + 128 * t
 constexpr float kRescaleLog2 = 8.0f;
 
 struct Params {
@@ -61,6 +67,8 @@ struct Params {
     const int32_t* block_tables;
     int32_t bt_stride, block_size, num_blocks;
     int32_t num_seqs, hq, hkv, group, q_blocks;
+    int32_t pair;   // 1: tiles A/B are two query heads of one kv head (even group); 0: rows r / r+128 of one head
+    int32_t slots;  // head slots per sequence: hq / 2 when pairing, else hq
     float scale_log2;
 };
 
@@ -72,6 +80,7 @@ struct Smem {
     uint64_t k_full[kKStages], k_empty[kKStages];
     uint64_t v_full[kVStages], v_empty[kVStages];
     uint64_t s_full[2], p_ready[2], o_done[2];  // per tile A/B
+    uint64_t s_free;                            // the S buffer has been read (one phase per S tile)
     uint64_t drain;
     uint32_t tmem_base;
     int32_t err;
@@ -79,8 +88,9 @@ struct Smem {
 
 __device__ int32_t g_prefill_error;  // bounded waits that gave up (diagnostics)
 
+template <bool SPIN = false>
 __device__ __forceinline__ bool wait_or_flag(uint64_t* bar, uint32_t parity, Smem& sm) {
-    if (mbar_wait(bar, parity)) return true;
+    if (SPIN ? mbar_wait_spin(bar, parity) : mbar_wait(bar, parity)) return true;
     atomicOr(&g_prefill_error, 1);
     *reinterpret_cast<volatile int32_t*>(&sm.err) = 1;
     return false;
@@ -94,9 +104,12 @@ __device__ __forceinline__ int key_tiles(int r0, int r1, int lq, int lk) {
     return (nkeys + kBN - 1) / kBN;
 }
 
-// One work unit: a 256-row query block (tiles A and B) of one head of one sequence.
+// One work unit: two 128-row query tiles A and B of one sequence that read the
+// same K/V tiles -- the same rows of two query heads of one kv head when the
+// group is even (both tiles see the same keys), else rows r and r + 128 of
+// one head.
 struct Unit {
-    int s, h, q0, lq, k0, lk, row0, nt[2], ntiles;
+    int s, q0, lq, k0, lk, h[2], row[2], nt[2], ntiles;
     bool has_b;
 };
 
@@ -109,21 +122,29 @@ __device__ __forceinline__ int unit_at(int k, int cta, int G) {
     return (k & 1) ? (k + 1) * G - 1 - cta : k * G + cta;
 }
 __device__ __forceinline__ bool load_unit(const Params& p, int u, Unit& w) {
-    const int per = p.num_seqs * p.hq;
+    const int per = p.num_seqs * p.slots;
     const int qb = p.q_blocks - 1 - u / per;
     const int rem = u - (u / per) * per;
-    w.s = rem / p.hq;
-    w.h = rem - w.s * p.hq;
+    w.s = rem / p.slots;
+    const int hs = rem - w.s * p.slots;
+    if (p.pair) {
+        w.h[0] = 2 * hs;
+        w.h[1] = 2 * hs + 1;
+        w.row[0] = w.row[1] = qb * kBM;
+    } else {
+        w.h[0] = w.h[1] = hs;
+        w.row[0] = qb * 2 * kBM;
+        w.row[1] = w.row[0] + kBM;
+    }
     w.q0 = p.cu_q[w.s];
     w.lq = p.cu_q[w.s + 1] - w.q0;
-    w.row0 = qb * 2 * kBM;
-    if (w.row0 >= w.lq) return false;
+    if (w.row[0] >= w.lq) return false;
     w.k0 = p.cu_k[w.s];
     w.lk = p.cu_k[w.s + 1] - w.k0;
-    w.nt[0] = key_tiles(w.row0, w.row0 + kBM, w.lq, w.lk);
-    w.nt[1] = key_tiles(w.row0 + kBM, w.row0 + 2 * kBM, w.lq, w.lk);
+    w.nt[0] = key_tiles(w.row[0], w.row[0] + kBM, w.lq, w.lk);
+    w.nt[1] = key_tiles(w.row[1], w.row[1] + kBM, w.lq, w.lk);
     w.ntiles = max(w.nt[0], w.nt[1]);
-    w.has_b = w.row0 + kBM < w.lq;
+    w.has_b = w.row[1] < w.lq;
     return true;
 }
 
@@ -132,15 +153,19 @@ __device__ __forceinline__ bool load_unit(const Params& p, int u, Unit& w) {
 // then P = 2^(S*scale - m) written back as bf16 over the S columns.  MASK
 // selects the bottom-right causal / sequence-end masking; tiles that lie
 // inside the row's visible range take the mask-free instantiation.
-template <bool MASK, bool BF16>
-__device__ __forceinline__ void softmax_tile(uint32_t s_col, int kbase, int limit, float sl2, float& m, float& alpha,
-                                             bool& rescale, float& sum) {
-    // One round trip to tensor memory: all 128 scores of the row in registers.
+template <bool BF16>
+__device__ __forceinline__ void softmax_tile(bool mask, uint32_t s_col, uint64_t* s_free, int kbase, int limit,
+                                             float sl2, float& m, float& alpha, bool& rescale, float& sum,
+                                             uint32_t (&pk)[kBN / 2]) {
+    // All 128 scores of the row in registers; the S buffer is released at once
+    // so that the next S tile (of either query tile) can be computed into it.
     float v[kBN];
 #pragma unroll
     for (int c = 0; c < kBN / 32; ++c) tc::tmem_ld32(s_col + c * 32, *reinterpret_cast<float(*)[32]>(&v[c * 32]));
     tc::tmem_wait_ld();
-    if (MASK) {
+    tc::fence_before_sync();
+    mbar_arrive(s_free);
+    if (mask) {
 #pragma unroll
         for (int e = 0; e < kBN; ++e)
             if (kbase + e > limit) v[e] = -INFINITY;
@@ -162,18 +187,12 @@ __device__ __forceinline__ void softmax_tile(uint32_t s_col, int kbase, int limi
     const float msl = m == -INFINITY ? 0.f : m * sl2;
     float sum4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int c2 = 0; c2 < kBN / 64; ++c2) {
-        uint32_t pk[32];
-#pragma unroll
-        for (int e = 0; e < 64; e += 2) {
-            // masked scores are -inf, and ex2 of -inf is +0
-            const float a = fast_exp2(fmaf(v[c2 * 64 + e], sl2, -msl));
-            const float b = fast_exp2(fmaf(v[c2 * 64 + e + 1], sl2, -msl));
-            sum4[(e >> 1) & 3] += a + b;
-            pk[e / 2] = pack2<BF16>(a, b);
-        }
-        // P for 64 keys occupies 32 TMEM columns at s_col + 32*c2 (over S, already read)
-        tc::tmem_st32(s_col + c2 * 32, pk);
+    for (int e = 0; e < kBN; e += 2) {
+        // masked scores are -inf, and ex2 of -inf is +0
+        const float a = fast_exp2(fmaf(v[e], sl2, -msl));
+        const float b = fast_exp2(fmaf(v[e + 1], sl2, -msl));
+        sum4[(e >> 1) & 3] += a + b;
+        pk[e / 2] = pack2<BF16>(a, b);
     }
     sum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
 }
@@ -185,7 +204,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     extern __shared__ uint8_t smem_raw[];
     Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int total_units = p.q_blocks * p.num_seqs * p.hq;
+    const int total_units = p.q_blocks * p.num_seqs * p.slots;
 
     if (tid == 0) {
         mbar_init(&sm.q_full, 1);
@@ -203,7 +222,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&sm.p_ready[i], 128);
             mbar_init(&sm.o_done[i], 1);
         }
-        mbar_init(&sm.drain, 1);
+        mbar_init(&sm.s_free, 128);
+        mbar_init(&sm.drain, 2);  // one commit per MMA issuer
         sm.err = 0;
         fence_mbar_init();
     }
@@ -249,13 +269,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (!wait_or_flag(&sm.q_empty, (nq & 1) ^ 1, sm)) break;
                         mbar_arrive_expect_tx(&sm.q_full, (w.has_b ? 4 : 2) * kHalf);
                         for (int t = 0; t < (w.has_b ? 2 : 1); ++t) {
-                            tma_load_2d(sm.q[t][0], &tmq, w.h * kD, w.q0 + w.row0 + t * kBM, &sm.q_full, pol_q);
-                            tma_load_2d(sm.q[t][1], &tmq, w.h * kD + 64, w.q0 + w.row0 + t * kBM, &sm.q_full, pol_q);
+                            tma_load_2d(sm.q[t][0], &tmq, w.h[t] * kD, w.q0 + w.row[t], &sm.q_full, pol_q);
+                            tma_load_2d(sm.q[t][1], &tmq, w.h[t] * kD + 64, w.q0 + w.row[t], &sm.q_full, pol_q);
                         }
                         ++nq;
                     }
                     const int32_t* bt = p.block_tables ? p.block_tables + int64_t(w.s) * p.bt_stride : nullptr;
-                    const int x = (w.h / p.group) * kD;
+                    const int x = (w.h[0] / p.group) * kD;
                     for (int j = 0; j < w.ntiles; ++j, ++g) {
                         const int st = g % NS;
                         if (failed() || !wait_or_flag(&empty[st], ((g / NS) & 1) ^ 1, sm)) break;
@@ -284,80 +304,81 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mbar_wait(&full[st], (last / NS) & 1);
                 }
             }
-        } else if (warp == kMmaWarp) {
-            // ------------------------------------------------------------ MMA issuer
+        } else if (warp == kMmaWarp || warp == kMmaWarp + 1) {
+            // ------------------------------------------------------------ MMA issuers
+            // Lane 0 of warp kMmaWarp issues every S = Q K^T MMA, lane 0 of warp
+            // kMmaWarp + 1 every O += P V MMA.  The two streams share no tensor memory
+            // (S buffer vs P / O columns), so neither waits on the other; one issuing
+            // thread sustains only about one 128x128x16 MMA per ~110 cycles, and two
+            // keep the tensor pipe busy.  Both walk the same units and key tiles.
             if (lane == 0) {
+                const bool s_issuer = warp == kMmaWarp;
                 constexpr uint32_t idS = tc::idesc_f16<BF16>(kBM, kBN, false, false);
                 constexpr uint32_t idPV = tc::idesc_f16<BF16>(kBM, kD, false, true);
                 int nq = 0, g = 0;
-                int npv[2] = {0, 0};  // P tiles consumed per query tile (across units)
+                int n_s = 0;              // S tiles issued (across units): the S buffer's uses
+                int npv[2] = {0, 0};      // PV tiles issued per query tile (across units)
                 bool ok = true;
-                auto issue_s = [&](int t, int kst) {
-                    const uint32_t qa = smem_u32(sm.q[t][0]);
-                    const uint32_t ka = smem_u32(sm.k[kst][0]);
-    #pragma unroll
-                    for (int kk = 0; kk < kD / 16; ++kk) {
-                        // K-major operands: 16 dims = 32 bytes inside a 128-byte swizzled row
-                        const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
-                        tc::mma_ss(tmem + t * 128, tc::smem_desc_sw128(qa + off, 16, 1024),
-                                   tc::smem_desc_sw128(ka + off, 16, 1024), idS, kk > 0 ? 1u : 0u);
-                    }
-                    tc::commit(&sm.s_full[t]);
-                };
-                auto issue_pv = [&](int t, int vst, bool first) {
-                    if (!wait_or_flag(&sm.p_ready[t], npv[t] & 1, sm)) return false;
-                    ++npv[t];
-                    tc::fence_after_sync();
-                    const uint32_t va = smem_u32(sm.v[vst][0]);
-    #pragma unroll
-                    for (int kk = 0; kk < kBN / 16; ++kk) {
-                        // V is MN-major: 16 keys = two 8-row swizzle atoms (SBO 1024 B); the
-                        // second 64 dims live in the V-hi half (LBO = kHalf).
-                        tc::mma_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8,
-                                   tc::smem_desc_sw128(va + kk * 16 * 128, kHalf, 1024), idPV,
-                                   (!first || kk > 0) ? 1u : 0u);
-                    }
-                    tc::commit(&sm.o_done[t]);
-                    return true;
-                };
-                // V tile of key tile g must have landed before its first PV.
-                auto wait_v = [&](int gg) { return wait_or_flag(&sm.v_full[gg % kVStages], (gg / kVStages) & 1, sm); };
                 Unit w;
                 for (int k = 0; ok; ++k) {
                     const int u = unit_at(k, blockIdx.x, gridDim.x);
                     if (u >= total_units || failed()) break;
                     if (!load_unit(p, u, w) || w.ntiles == 0) continue;
-                    if (!wait_or_flag(&sm.q_full, nq & 1, sm)) { ok = false; break; }
-                    ++nq;
-                    tc::fence_after_sync();
                     const int g0 = g;
-                    for (int j = 0; j < w.ntiles; ++j) {
-                        const int gj = g0 + j, kst = gj % kKStages, pvs = (gj - 1) % kVStages;
-                        if (!wait_or_flag(&sm.k_full[kst], (gj / kKStages) & 1, sm)) { ok = false; break; }
-                        if (j > 0 && !wait_v(gj - 1)) { ok = false; break; }
+                    if (s_issuer) {
+                        if (!wait_or_flag(&sm.q_full, nq & 1, sm)) { ok = false; break; }
+                        ++nq;
                         tc::fence_after_sync();
-                        // tile A: PV(j-1) frees S_A before S_A(j) overwrites it (in-order tensor pipe)
-                        if (j < w.nt[0]) {
-                            if (j > 0 && !issue_pv(0, pvs, j == 1)) { ok = false; break; }
-                            issue_s(0, kst);
-                        } else if (j == w.nt[0] && j > 0) {
-                            if (!issue_pv(0, pvs, j == 1)) { ok = false; break; }
+                        for (int j = 0; j < w.ntiles && ok; ++j) {
+                            const int gj = g0 + j, kst = gj % kKStages;
+                            if (!wait_or_flag(&sm.k_full[kst], (gj / kKStages) & 1, sm)) { ok = false; break; }
+                            tc::fence_after_sync();
+                            const uint32_t ka = smem_u32(sm.k[kst][0]);
+                            for (int t = 0; t < 2; ++t) {
+                                if (j >= w.nt[t]) continue;
+                                // the previous S tile must have been read out of the buffer
+                                if (n_s > 0 && !wait_or_flag(&sm.s_free, (n_s - 1) & 1, sm)) { ok = false; break; }
+                                ++n_s;
+                                tc::fence_after_sync();
+                                const uint32_t qa = smem_u32(sm.q[t][0]);
+#pragma unroll
+                                for (int kk = 0; kk < kD / 16; ++kk) {
+                                    // K-major operands: 16 dims = 32 bytes inside a 128-byte swizzled row
+                                    const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
+                                    tc::mma_ss(tmem + kColS, tc::smem_desc_sw128(qa + off, 16, 1024),
+                                               tc::smem_desc_sw128(ka + off, 16, 1024), idS, kk > 0 ? 1u : 0u);
+                                }
+                                tc::commit(&sm.s_full[t]);
+                            }
+                            if (!ok) break;
+                            tc::commit(&sm.k_empty[kst]);                  // both S of key tile j done
+                            if (j == w.ntiles - 1) tc::commit(&sm.q_empty);  // last S of the unit done
                         }
-                        if (j < w.nt[1]) {
-                            if (j > 0 && !issue_pv(1, pvs, j == 1)) { ok = false; break; }
-                            issue_s(1, kst);
+                    } else {
+                        for (int j = 0; j < w.ntiles && ok; ++j) {
+                            const int gj = g0 + j, vst = gj % kVStages;
+                            if (!wait_or_flag(&sm.v_full[vst], (gj / kVStages) & 1, sm)) { ok = false; break; }
+                            const uint32_t va = smem_u32(sm.v[vst][0]);
+                            for (int t = 0; t < 2; ++t) {
+                                if (j >= w.nt[t]) continue;
+                                if (!wait_or_flag(&sm.p_ready[t], npv[t] & 1, sm)) { ok = false; break; }
+                                ++npv[t];
+                                tc::fence_after_sync();
+#pragma unroll
+                                for (int kk = 0; kk < kBN / 16; ++kk) {
+                                    // P (K-major, 16 keys = 8 columns of bf16 pairs) from tensor memory;
+                                    // V is MN-major: 16 keys = two 8-row swizzle atoms (SBO 1024 B), the
+                                    // second 64 dims in the V-hi half (LBO = kHalf).
+                                    tc::mma_ts(tmem + kColO + t * 128, tmem + kColP + t * 64 + kk * 8,
+                                               tc::smem_desc_sw128(va + kk * 16 * 128, kHalf, 1024), idPV,
+                                               (j > 0 || kk > 0) ? 1u : 0u);
+                                }
+                                tc::commit(&sm.o_done[t]);
+                            }
+                            if (!ok) break;
+                            tc::commit(&sm.v_empty[vst]);  // both PV of key tile j done
                         }
-                        tc::commit(&sm.k_empty[kst]);                  // both S of tile j issued
-                        if (j == w.ntiles - 1) tc::commit(&sm.q_empty);  // last S of the unit issued
-                        if (j > 0) tc::commit(&sm.v_empty[pvs]);       // both PVs of tile j-1 issued
                     }
-                    if (!ok) break;
-                    const int gl = g0 + w.ntiles - 1, lvs = gl % kVStages;
-                    if (!wait_v(gl)) { ok = false; break; }
-                    tc::fence_after_sync();
-                    if (w.nt[0] == w.ntiles && !issue_pv(0, lvs, w.ntiles == 1)) { ok = false; break; }
-                    if (w.nt[1] == w.ntiles && !issue_pv(1, lvs, w.ntiles == 1)) { ok = false; break; }
-                    tc::commit(&sm.v_empty[lvs]);
                     g = g0 + w.ntiles;
                 }
                 // Wait (bounded) for every MMA issued above before the tensor memory is freed.
@@ -372,10 +393,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int quarter = warp & 3;     // TMEM lanes 32*quarter .. +31 belong to this warp
         const int r = quarter * 32 + lane;
         const uint32_t lane_addr = uint32_t(quarter * 32) << 16;
-        const uint32_t s_col = tmem + lane_addr + t * 128;
-        const uint32_t o_col = tmem + lane_addr + 256 + t * 128;
+        const uint32_t s_col = tmem + lane_addr + kColS;
+        const uint32_t p_col = tmem + lane_addr + kColP + t * 64;
+        const uint32_t o_col = tmem + lane_addr + kColO + t * 128;
         const float sl2 = p.scale_log2;
-        int ns = 0;  // S tiles of this query tile consumed (across units) = PVs issued for it
+        int ns = 0;  // S tiles of this query tile consumed (across units) = P tiles written
         int g = 0;   // K/V tiles streamed so far (across units), to find a tile's stage
         Unit w;
         for (int k = 0;; ++k) {
@@ -384,9 +406,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!load_unit(p, u, w)) continue;
             const int g0 = g;
             g += w.ntiles;
-            const int qrow = w.row0 + t * kBM + r;
+            const int qrow = w.row[t] + r;
             const int my_tiles = w.nt[t];
-            uint4* dst = reinterpret_cast<uint4*>(p.out + int64_t(w.q0 + qrow) * p.out_stride + w.h * kD);
+            uint4* dst = reinterpret_cast<uint4*>(p.out + int64_t(w.q0 + qrow) * p.out_stride + w.h[t] * kD);
             if (my_tiles == 0) {  // rows that see no key at all (only when lk < lq)
                 if (qrow < w.lq)
                     for (int c = 0; c < kD / 8; ++c) dst[c] = make_uint4(0, 0, 0, 0);
@@ -406,28 +428,30 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const bool full_row = __all_sync(0xffffffffu, kbase + kBN - 1 <= limit);
                 float alpha, sum;
                 bool rescale;
-                if (full_row)
-                    softmax_tile<false, BF16>(s_col, kbase, limit, sl2, m, alpha, rescale, sum);
-                else
-                    softmax_tile<true, BF16>(s_col, kbase, limit, sl2, m, alpha, rescale, sum);
+                uint32_t pk[kBN / 2];
+                softmax_tile<BF16>(!full_row, s_col, &sm.s_free, kbase, limit, sl2, m, alpha, rescale, sum, pk);
                 l = fmaf(l, alpha, sum);
-                // Warp-collective O rescale when any row of the warp needs it (alpha = 1 elsewhere).
-                if (__any_sync(0xffffffffu, rescale && j > 0)) {
-                    if (!(rescale && j > 0)) alpha = 1.f;
-                    // O must hold PV(j-1) of this unit before it is scaled.
+                if (j > 0) {
+                    // PV(j-1) must have read P and written O before P is overwritten or O scaled.
                     if (!wait_or_flag(&sm.o_done[t], (ns0 + j - 1) & 1, sm)) { ok = false; break; }
                     tc::fence_after_sync();
+                    // Warp-collective O rescale when any row of the warp needs it (alpha = 1 elsewhere).
+                    if (__any_sync(0xffffffffu, rescale)) {
+                        if (!rescale) alpha = 1.f;
 #pragma unroll 1
-                    for (int c = 0; c < kD / 32; ++c) {
-                        float o[32];
-                        tc::tmem_ld32(o_col + c * 32, o);
-                        tc::tmem_wait_ld();
-                        uint32_t uo[32];
+                        for (int c = 0; c < kD / 32; ++c) {
+                            float o[32];
+                            tc::tmem_ld32(o_col + c * 32, o);
+                            tc::tmem_wait_ld();
+                            uint32_t uo[32];
 #pragma unroll
-                        for (int e = 0; e < 32; ++e) uo[e] = __float_as_uint(o[e] * alpha);
-                        tc::tmem_st32(o_col + c * 32, uo);
+                            for (int e = 0; e < 32; ++e) uo[e] = __float_as_uint(o[e] * alpha);
+                            tc::tmem_st32(o_col + c * 32, uo);
+                        }
                     }
                 }
+                tc::tmem_st32(p_col, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
+                tc::tmem_st32(p_col + 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
                 tc::tmem_wait_st();
                 // Cache rows past this sequence's keys may hold NaN bits; P is 0 there but
                 // 0 * NaN is NaN, so the first tile to use the stage clears those V rows.
@@ -514,10 +538,16 @@ extern "C" int32_t b200_varlen_prefill(void* out, const void* q, int64_t q_strid
         B200_REQUIRE(block_table_stride > 0, "varlen_prefill: block_table_stride %d", block_table_stride);
         B200_REQUIRE(total_k_rows % block_size == 0, "varlen_prefill: cache rows %d not whole blocks", total_k_rows);
     }
-    const int q_blocks = (max_seqlen_q + 2 * kBM - 1) / (2 * kBM);
-    if (int64_t(q_blocks) * num_seqs * num_heads > INT32_MAX / 2)
-        return fail(B200_ERR_UNSUPPORTED, "varlen_prefill: %d query blocks x %d sequences x %d heads", q_blocks,
-                    num_seqs, num_heads);
+    // Even GQA groups pair two query heads per unit (same rows, same keys: the
+    // tiles stay in step); otherwise a unit is 256 rows of one head.
+    const int group = num_heads / num_kv_heads;
+    const bool pair = group % 2 == 0;
+    const int slots = pair ? num_heads / 2 : num_heads;
+    const int rows_per_unit = pair ? kBM : 2 * kBM;
+    const int q_blocks = (max_seqlen_q + rows_per_unit - 1) / rows_per_unit;
+    if (int64_t(q_blocks) * num_seqs * slots > INT32_MAX / 2)
+        return fail(B200_ERR_UNSUPPORTED, "varlen_prefill: %d query blocks x %d sequences x %d head slots", q_blocks,
+                    num_seqs, slots);
     const bool bf16 = dtype == B200_BF16;
     // The tensor maps span exactly the caller's q / k / v rows, so a tile that
     // runs past the last token reads the TMA fill value (zero), never memory
@@ -546,14 +576,16 @@ extern "C" int32_t b200_varlen_prefill(void* out, const void* q, int64_t q_strid
     prm.num_seqs = num_seqs;
     prm.hq = num_heads;
     prm.hkv = num_kv_heads;
-    prm.group = num_heads / num_kv_heads;
+    prm.group = group;
     prm.q_blocks = q_blocks;
+    prm.pair = pair ? 1 : 0;
+    prm.slots = slots;
     prm.scale_log2 = softmax_scale * 1.4426950408889634f;
 
     const int smem = int(sizeof(Smem)) + 1024;
     const void* fn = bf16 ? (const void*)prefill_kernel<true> : (const void*)prefill_kernel<false>;
     ensure_smem_attr(fn, smem);
-    const int64_t units = int64_t(q_blocks) * num_seqs * num_heads;
+    const int64_t units = int64_t(q_blocks) * num_seqs * slots;
     const dim3 grid(unsigned(units < device_sm_count() ? units : device_sm_count()));
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (bf16) prefill_kernel<true><<<grid, kThreads, smem, st>>>(prm, tmq, tmk, tmv);

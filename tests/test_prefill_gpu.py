@@ -29,7 +29,7 @@ def run_packed(pkg, c, dtype=torch.bfloat16, strided_v=False):
 
 
 @pytest.mark.parametrize("lens", [[1], [9], [127], [128], [129], [300, 1, 57], [1000], [64, 512, 257, 2, 130]])
-@pytest.mark.parametrize("hq,hkv", [(16, 8), (16, 16), (8, 1)])
+@pytest.mark.parametrize("hq,hkv", [(16, 8), (16, 16), (8, 1), (12, 4), (32, 8)])
 def test_packed_against_oracle(pkg, lens, hq, hkv):
     c = cases.make_prefill_case(lens, hq, hkv, seed=sum(lens) + hq)
     got = run_packed(pkg, c)
