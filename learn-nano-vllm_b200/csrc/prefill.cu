@@ -148,11 +148,12 @@ __device__ __forceinline__ bool load_unit(const Params& p, int u, Unit& w) {
     return true;
 }
 
-// One row's share of a key tile: max over its 128 scores in tensor memory,
-// lazy update of the running max m (new max only when it grows by > 2^8),
-// then P = 2^(S*scale - m) written back as bf16 over the S columns.  MASK
-// selects the bottom-right causal / sequence-end masking; tiles that lie
-// inside the row's visible range take the mask-free instantiation.
+// One row's share of a key tile: its 128 scores are read from the S buffer
+// into registers (the buffer is released at once), the max is taken, the
+// running max m is updated lazily (only when it grows by > 2^8), and
+// P = 2^(S*scale - m) is packed to bf16 pairs in pk for the caller to store.
+// `mask` applies the bottom-right causal / sequence-end masking (diagonal and
+// tail tiles only).
 template <bool BF16>
 __device__ __forceinline__ void softmax_tile(bool mask, uint32_t s_col, uint64_t* s_free, int kbase, int limit,
                                              float sl2, float& m, float& alpha, bool& rescale, float& sum,
@@ -170,13 +171,14 @@ __device__ __forceinline__ void softmax_tile(bool mask, uint32_t s_col, uint64_t
         for (int e = 0; e < kBN; ++e)
             if (kbase + e > limit) v[e] = -INFINITY;
     }
-    float m8[8];
+    // four chains of three-input max over the row
+    float m4[4] = {v[0], v[1], v[2], v[3]};
 #pragma unroll
-    for (int e = 0; e < 8; ++e) m8[e] = v[e];
+    for (int e = 4; e < kBN - 4; e += 8)
 #pragma unroll
-    for (int e = 8; e < kBN; ++e) m8[e & 7] = fmaxf(m8[e & 7], v[e]);
+        for (int c = 0; c < 4; ++c) m4[c] = max3f(m4[c], v[e + 2 * c], v[e + 2 * c + 1]);
     const float mx =
-        fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+        max3f(max3f(m4[0], m4[1], v[kBN - 4]), max3f(m4[2], m4[3], v[kBN - 3]), fmaxf(v[kBN - 2], v[kBN - 1]));
     alpha = 1.f;
     rescale = false;
     if (mx != -INFINITY && (m == -INFINITY || (mx - m) * sl2 > kRescaleLog2)) {
@@ -185,16 +187,19 @@ __device__ __forceinline__ void softmax_tile(bool mask, uint32_t s_col, uint64_t
         m = mx;
     }
     const float msl = m == -INFINITY ? 0.f : m * sl2;
-    float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+    // pairs of scores through packed fma / add (half the issue slots of scalar code)
+    float2 s2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+    const float2 sl22 = make_float2(sl2, sl2), nmsl = make_float2(-msl, -msl);
 #pragma unroll
     for (int e = 0; e < kBN; e += 2) {
+        const float2 x = ffma2(make_float2(v[e], v[e + 1]), sl22, nmsl);
         // masked scores are -inf, and ex2 of -inf is +0
-        const float a = fast_exp2(fmaf(v[e], sl2, -msl));
-        const float b = fast_exp2(fmaf(v[e + 1], sl2, -msl));
-        sum4[(e >> 1) & 3] += a + b;
-        pk[e / 2] = pack2<BF16>(a, b);
+        const float2 y = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+        s2[(e >> 1) & 3] = fadd2(s2[(e >> 1) & 3], y);
+        pk[e / 2] = pack2<BF16>(y.x, y.y);
     }
-    sum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
+    const float2 st = fadd2(fadd2(s2[0], s2[1]), fadd2(s2[2], s2[3]));
+    sum = st.x + st.y;
 }
 
 template <bool BF16>
