@@ -17,9 +17,17 @@
 //   sampling: inverse CDF over tile sums, thread sums of the chosen tile,
 //              then the thread's 16 elements, each scanned left to right.
 //
-// Kernel 1 (one CTA per logits row, one pass over the row): M and S.
-// Kernel 2 (one CTA per sequence): decisions from the per-row statistics,
-// then one pass over the rejected row (residual) or the bonus row.
+// Four launches, each spread over the whole GPU:
+//   1. tile_stats (one CTA per logits row x 4096-value tile): M_t and S_t;
+//   2. decide (one CTA per sequence): M and S of the sequence's 2k+1 rows
+//      from their tile statistics, the accept/reject decisions and the row
+//      to sample from;
+//   3. weights (one CTA per sequence x tile): the fixed-order thread partials
+//      and tile sums of the sampling weights -- the residual max(p - q, 0)
+//      and p itself (the fallback when the residual has no mass);
+//   4. pick (one thread per sequence): the inverse-CDF scans.
+// Every sum keeps the order stated above, so splitting the work over CTAs
+// changes no result.
 #include "common.cuh"
 
 namespace b200 {
@@ -89,56 +97,39 @@ __device__ __forceinline__ void load_tile(const float* x, int V, int t, float T,
     }
 }
 
-// Per row: M_t and S_t = fixed-order tile sum of exp_c(x - M_t) for every
-// tile, then M = max M_t and S = sum_t S_t * exp_c(M_t - M).  Each row is read
-// once; the next tile's loads are issued before the current tile's reductions.
-__global__ void __launch_bounds__(kThreads) row_stats_kernel(Rows R, float2* stats) {
+// One tile of one row: M_t = tile max and S_t = the fixed-order tile sum of
+// exp_c(x - M_t) over the tile's finite values.
+__global__ void __launch_bounds__(kThreads) tile_stats_kernel(Rows R, float2* tstats, int nt) {
     __shared__ float wred[kThreads / 32];
-    __shared__ float tile_m[kMaxTiles], tile_s[kMaxTiles];
+    const int row = blockIdx.x / nt, t = blockIdx.x - row * nt;
     int b;
-    const float* x = row_ptr(R, blockIdx.x, &b);
+    const float* x = row_ptr(R, row, &b);
     const float T = R.temps ? R.temps[b] : 0.f;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const bool vec = (R.V & 3) == 0;
-    const int nt = (R.V + kTileElems - 1) / kTileElems;
-    float cur[16], nxt[16];
-    load_tile(x, R.V, 0, T, vec, cur);
-    for (int t = 0; t < nt; ++t) {
-        if (t + 1 < nt) load_tile(x, R.V, t + 1, T, vec, nxt);
-        float m = -INFINITY;
+    float v[16];
+    load_tile(x, R.V, t, T, (R.V & 3) == 0, v);
+    float m = -INFINITY;
 #pragma unroll
-        for (int e = 0; e < 16; ++e) m = fmaxf(m, cur[e]);
+    for (int e = 0; e < 16; ++e) m = fmaxf(m, v[e]);
 #pragma unroll
-        for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        if (lane == 0) wred[warp] = m;
-        __syncthreads();
-        float Mt = wred[0];
+    for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) wred[warp] = m;
+    __syncthreads();
+    float Mt = wred[0];
 #pragma unroll
-        for (int w = 1; w < kThreads / 32; ++w) Mt = fmaxf(Mt, wred[w]);
-        __syncthreads();
-        float acc = 0.f;
+    for (int w = 1; w < kThreads / 32; ++w) Mt = fmaxf(Mt, wred[w]);
+    __syncthreads();
+    float acc = 0.f;
 #pragma unroll
-        for (int e = 0; e < 16; ++e)
-            if (isfinite(cur[e])) acc = __fadd_rn(acc, exp_c(__fsub_rn(cur[e], Mt)));
-        const float ws = warp_butterfly(acc);
-        if (lane == 0) wred[warp] = ws;
-        __syncthreads();
-        if (tid == 0) {
-            float st = 0.f;
-            for (int w = 0; w < kThreads / 32; ++w) st = __fadd_rn(st, wred[w]);
-            tile_m[t] = Mt;
-            tile_s[t] = st;
-        }
-        __syncthreads();
-#pragma unroll
-        for (int e = 0; e < 16; ++e) cur[e] = nxt[e];
-    }
+    for (int e = 0; e < 16; ++e)
+        if (isfinite(v[e])) acc = __fadd_rn(acc, exp_c(__fsub_rn(v[e], Mt)));
+    const float ws = warp_butterfly(acc);
+    if (lane == 0) wred[warp] = ws;
+    __syncthreads();
     if (tid == 0) {
-        float M = -INFINITY;
-        for (int t = 0; t < nt; ++t) M = fmaxf(M, tile_m[t]);
-        float S = 0.f;
-        for (int t = 0; t < nt; ++t) S = __fadd_rn(S, __fmul_rn(tile_s[t], exp_c(__fsub_rn(tile_m[t], M))));
-        stats[blockIdx.x] = make_float2(M, S);
+        float st = 0.f;
+        for (int w = 0; w < kThreads / 32; ++w) st = __fadd_rn(st, wred[w]);
+        tstats[blockIdx.x] = make_float2(Mt, st);
     }
 }
 
@@ -172,191 +163,257 @@ __device__ int scan_pick(const float* vals, int n, float target, float acc0, flo
 
 struct Decide {
     Rows R;
-    const float2* stats;
+    const float2* tstats;  // [rows][nt]
     const int32_t* draft;
     const float* ua;
     const float* us;
     int32_t* out_tokens;
     int32_t* out_num;
+    int32_t nt;
 };
 
-// Weight of token j for the sampling row: the residual max(p - q, 0) or p.
+// Per sequence: the row to sample from and its normalisers.
+struct PickInfo {
+    int32_t rej;
+    float Mt, St, Md, Sd;
+    int32_t pad[3];
+};
+
+// Weight of token j for the sampling row: p, and the residual max(p - q, 0).
 struct Weight {
     const float *xt, *xd;
     float T, Mt, St, Md, Sd;
-    bool residual;
-    bool vec;
-    __device__ __forceinline__ float from(float lt, float ld) const {
-        const float p = __fdiv_rn(exp_c(__fsub_rn(scaled(lt, T), Mt)), St);
-        if (!residual) return p;
+    __device__ __forceinline__ float p(float lt) const { return __fdiv_rn(exp_c(__fsub_rn(scaled(lt, T), Mt)), St); }
+    __device__ __forceinline__ float residual(float pv, float ld) const {
         const float q = __fdiv_rn(exp_c(__fsub_rn(scaled(ld, T), Md)), Sd);
-        return fmaxf(__fsub_rn(p, q), 0.f);
-    }
-    __device__ __forceinline__ float operator()(int j) const {
-        return from(__ldg(xt + j), residual ? __ldg(xd + j) : 0.f);
+        return fmaxf(__fsub_rn(pv, q), 0.f);
     }
 };
 
-// Fixed-order thread partial of tile t with float4 loads of both rows.
-__device__ __forceinline__ float weight_partial(const Weight& w, int t, int V) {
-    float lt[16], ld[16];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const int base = t * kTileElems + k * 1024 + 4 * int(threadIdx.x);
-        if (w.vec && base + 3 < V) {
-            const float4 a = __ldg(reinterpret_cast<const float4*>(w.xt + base));
-            lt[4 * k] = a.x, lt[4 * k + 1] = a.y, lt[4 * k + 2] = a.z, lt[4 * k + 3] = a.w;
-            if (w.residual) {
-                const float4 c = __ldg(reinterpret_cast<const float4*>(w.xd + base));
-                ld[4 * k] = c.x, ld[4 * k + 1] = c.y, ld[4 * k + 2] = c.z, ld[4 * k + 3] = c.w;
-            } else {
-                ld[4 * k] = ld[4 * k + 1] = ld[4 * k + 2] = ld[4 * k + 3] = 0.f;
-            }
-        } else {
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                const bool in = base + c < V;
-                lt[4 * k + c] = in ? __ldg(w.xt + base + c) : 0.f;
-                ld[4 * k + c] = in && w.residual ? __ldg(w.xd + base + c) : 0.f;
-            }
-        }
-    }
-    float acc = 0.f;
-#pragma unroll
-    for (int e = 0; e < 16; ++e) {
-        const int j = t * kTileElems + (e >> 2) * 1024 + 4 * int(threadIdx.x) + (e & 3);
-        if (j < V) acc = __fadd_rn(acc, w.from(lt[e], ld[e]));
-    }
-    return acc;
+// M and S of row `row` from its tile statistics (tiles left to right).
+__device__ __forceinline__ float2 combine_row(const float2* ts, int nt) {
+    float M = -INFINITY;
+    for (int t = 0; t < nt; ++t) M = fmaxf(M, ts[t].x);
+    float S = 0.f;
+    for (int t = 0; t < nt; ++t) S = __fadd_rn(S, __fmul_rn(ts[t].y, exp_c(__fsub_rn(ts[t].x, M))));
+    return make_float2(M, S);
 }
 
-// Canonical inverse-CDF pick over the whole row; -1 if the row has no mass.
-__device__ int canon_pick(const Weight& w, int V, float u, float* part, float* wsum) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int nt = (V + kTileElems - 1) / kTileElems;
-    for (int t = 0; t < nt; ++t) {
-        const float pt = weight_partial(w, t, V);
-        part[t * kThreads + tid] = pt;
-        const float ws = warp_butterfly(pt);
-        if (lane == 0) wsum[t * (kThreads / 32) + warp] = ws;
-    }
-    __syncthreads();
-    __shared__ int pick;
-    if (tid == 0) {
-        float tsum[kMaxTiles];
-        float R = 0.f;
-        for (int t = 0; t < nt; ++t) {
-            float st = 0.f;
-            for (int x = 0; x < kThreads / 32; ++x) st = __fadd_rn(st, wsum[t * (kThreads / 32) + x]);
-            tsum[t] = st;
-            R = __fadd_rn(R, st);
-        }
-        const float target = __fmul_rn(u, R);
-        float acc;
-        int res = -1;
-        const int t = scan_pick(tsum, nt, target, 0.f, &acc);
-        if (t >= 0) {
-            const int i = scan_pick(part + t * kThreads, kThreads, target, acc, &acc);
-            if (i >= 0) {
-                float v16[16];
-                int idx[16];
-                for (int k = 0; k < 4; ++k)
-                    for (int c = 0; c < 4; ++c) {
-                        const int j = t * kTileElems + k * 1024 + 4 * i + c;
-                        idx[k * 4 + c] = j;
-                        v16[k * 4 + c] = j < V ? w(j) : 0.f;
-                    }
-                const int e = scan_pick(v16, 16, target, acc, &acc);
-                res = e < 0 ? -1 : idx[e];
-            }
-        }
-        pick = res;
-    }
-    __syncthreads();
-    const int r = pick;
-    __syncthreads();
-    return r;
-}
+constexpr int kDecideThreads = 128;  // >= 2 * 32 + 1 rows per sequence
 
-__global__ void __launch_bounds__(kThreads) decide_kernel(Decide d) {
-    extern __shared__ float dyn[];
+__global__ void __launch_bounds__(kDecideThreads) decide_kernel(Decide d, PickInfo* info) {
     const Rows& R = d.R;
     const int b = blockIdx.x, k = R.k, V = R.V;
-    const int nt = (V + kTileElems - 1) / kTileElems;
-    float* part = dyn;                      // [nt][256]
-    float* wsum = dyn + nt * kThreads;      // [nt][8]
-    __shared__ int rej_s;
-    const float T = R.temps ? R.temps[b] : 0.f;
     const int rows_t = R.B * (k + 1);
-    // Draft position i's decision on lane i (at most 32 drafts), then the
-    // first rejection in order.
+    __shared__ float2 ms[2 * 32 + 1];  // target rows 0..k, then draft rows 0..k-1
     __shared__ int accept_s[32];
-    if (threadIdx.x < k) {
-        const int i = threadIdx.x;
-        const int x = d.draft[b * k + i];
-        bool acc = false;
-        if (x >= 0 && x < V) {
-            const float2 st = d.stats[b * (k + 1) + i];
-            const float2 sd = d.stats[rows_t + b * k + i];
-            const float* xt = R.tl + (int64_t(b) * (k + 1) + i) * V;
-            const float* xd = R.dl + (int64_t(b) * k + i) * V;
-            const float p = __fdiv_rn(exp_c(__fsub_rn(scaled(xt[x], T), st.x)), st.y);
-            const float q = __fdiv_rn(exp_c(__fsub_rn(scaled(xd[x], T), sd.x)), sd.y);
-            acc = q > 0.f ? (d.ua[b * k + i] < fminf(1.f, __fdiv_rn(p, q))) : (p > 0.f);
-        }
-        accept_s[i] = acc;
+    const int r = threadIdx.x;
+    if (r < 2 * k + 1) {
+        const int row = r <= k ? b * (k + 1) + r : rows_t + b * k + (r - k - 1);
+        ms[r] = combine_row(d.tstats + int64_t(row) * d.nt, d.nt);
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
+    const float T = R.temps ? R.temps[b] : 0.f;
+    // Draft position i's decision on thread i, then the first rejection in order.
+    if (r < k) {
+        const int x = d.draft[b * k + r];
+        bool acc = false;
+        if (x >= 0 && x < V) {
+            const float2 st = ms[r], sd = ms[k + 1 + r];
+            const float* xt = R.tl + (int64_t(b) * (k + 1) + r) * V;
+            const float* xd = R.dl + (int64_t(b) * k + r) * V;
+            const float p = __fdiv_rn(exp_c(__fsub_rn(scaled(xt[x], T), st.x)), st.y);
+            const float q = __fdiv_rn(exp_c(__fsub_rn(scaled(xd[x], T), sd.x)), sd.y);
+            acc = q > 0.f ? (d.ua[b * k + r] < fminf(1.f, __fdiv_rn(p, q))) : (p > 0.f);
+        }
+        accept_s[r] = acc;
+    }
+    __syncthreads();
+    if (r == 0) {
         int rej = k;
         for (int i = 0; i < k; ++i)
             if (!accept_s[i]) {
                 rej = i;
                 break;
             }
-        rej_s = rej;
-    }
-    __syncthreads();
-    const int rej = rej_s;
-    Weight w;
-    w.T = T;
-    w.xt = R.tl + (int64_t(b) * (k + 1) + rej) * V;
-    const float2 st = d.stats[b * (k + 1) + rej];
-    w.Mt = st.x;
-    w.St = st.y;
-    w.residual = rej < k;
-    w.vec = (V & 3) == 0;
-    if (rej < k) {
-        w.xd = R.dl + (int64_t(b) * k + rej) * V;
-        const float2 sd = d.stats[rows_t + b * k + rej];
-        w.Md = sd.x;
-        w.Sd = sd.y;
-    } else {
-        w.xd = nullptr;
-        w.Md = w.Sd = 0.f;
-    }
-    const float u = d.us[b];
-    int tok = canon_pick(w, V, u, part, wsum);
-    if (tok < 0 && w.residual) {
-        w.residual = false;
-        tok = canon_pick(w, V, u, part, wsum);
-    }
-    if (tok < 0) tok = 0;
-    if (threadIdx.x == 0) {
+        PickInfo pi;
+        pi.rej = rej;
+        pi.Mt = ms[rej].x;
+        pi.St = ms[rej].y;
+        pi.Md = rej < k ? ms[k + 1 + rej].x : 0.f;
+        pi.Sd = rej < k ? ms[k + 1 + rej].y : 0.f;
+        pi.pad[0] = pi.pad[1] = pi.pad[2] = 0;
+        info[b] = pi;
+        // accepted drafts and the padding; the sampled token at `rej` comes from pick_kernel
         for (int i = 0; i <= k; ++i)
-            d.out_tokens[b * (k + 1) + i] = i < rej ? d.draft[b * k + i] : (i == rej ? tok : -1);
+            if (i != rej) d.out_tokens[b * (k + 1) + i] = i < rej ? d.draft[b * k + i] : -1;
         d.out_num[b] = rej + 1;
     }
+}
+
+__device__ __forceinline__ Weight make_weight(const Rows& R, const PickInfo& pi, int b) {
+    Weight w;
+    w.T = R.temps ? R.temps[b] : 0.f;
+    w.xt = R.tl + (int64_t(b) * (R.k + 1) + pi.rej) * R.V;
+    w.xd = pi.rej < R.k ? R.dl + (int64_t(b) * R.k + pi.rej) * R.V : nullptr;
+    w.Mt = pi.Mt;
+    w.St = pi.St;
+    w.Md = pi.Md;
+    w.Sd = pi.Sd;
+    return w;
+}
+
+// One tile of one sequence's sampling row: thread partials and tile sums of
+// the residual (slot 0, when the sequence rejected a draft) and of p (slot 1).
+// part [B][nt][2][256], tsum [B][nt][2].
+__global__ void __launch_bounds__(kThreads) weights_kernel(Rows R, const PickInfo* info, int nt, float* part,
+                                                           float* tsum) {
+    __shared__ float wred[2][kThreads / 32];
+    const int b = blockIdx.x / nt, t = blockIdx.x - b * nt;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, V = R.V;
+    const PickInfo pi = info[b];
+    const Weight w = make_weight(R, pi, b);
+    const bool res = pi.rej < R.k;
+    const bool vec = (V & 3) == 0;
+    float lt[16], ld[16];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int base = t * kTileElems + k * 1024 + 4 * tid;
+        if (vec && base + 3 < V) {
+            const float4 a = __ldg(reinterpret_cast<const float4*>(w.xt + base));
+            lt[4 * k] = a.x, lt[4 * k + 1] = a.y, lt[4 * k + 2] = a.z, lt[4 * k + 3] = a.w;
+            if (res) {
+                const float4 c = __ldg(reinterpret_cast<const float4*>(w.xd + base));
+                ld[4 * k] = c.x, ld[4 * k + 1] = c.y, ld[4 * k + 2] = c.z, ld[4 * k + 3] = c.w;
+            }
+        } else {
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const bool in = base + c < V;
+                lt[4 * k + c] = in ? __ldg(w.xt + base + c) : 0.f;
+                if (res) ld[4 * k + c] = in ? __ldg(w.xd + base + c) : 0.f;
+            }
+        }
+    }
+    float acc_r = 0.f, acc_p = 0.f;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+        const int j = t * kTileElems + (e >> 2) * 1024 + 4 * tid + (e & 3);
+        if (j < V) {
+            const float pv = w.p(lt[e]);
+            acc_p = __fadd_rn(acc_p, pv);
+            if (res) acc_r = __fadd_rn(acc_r, w.residual(pv, ld[e]));
+        }
+    }
+    float* pp = part + (int64_t(b) * nt + t) * 2 * kThreads;
+    pp[tid] = acc_r;
+    pp[kThreads + tid] = acc_p;
+    const float wr = warp_butterfly(acc_r), wp = warp_butterfly(acc_p);
+    if (lane == 0) {
+        wred[0][warp] = wr;
+        wred[1][warp] = wp;
+    }
+    __syncthreads();
+    if (tid < 2) {
+        float st = 0.f;
+        for (int x = 0; x < kThreads / 32; ++x) st = __fadd_rn(st, wred[tid][x]);
+        tsum[(int64_t(b) * nt + t) * 2 + tid] = st;
+    }
+}
+
+// Inverse-CDF pick over one slot's partials (one CTA of kThreads per
+// sequence); -1 if that weight row has no mass.  The scans are the serial
+// left-to-right ones of the definition, run by thread 0 over values staged in
+// shared memory.
+__device__ int pick_slot(const Weight& w, bool residual, int V, int nt, const float* part, const float* tsum, int slot,
+                         float u, float* sh_t, float* sh_p, float* sh_w, int* sh_i) {
+    const int tid = threadIdx.x;
+    if (tid < nt) sh_t[tid] = tsum[tid * 2 + slot];
+    __syncthreads();
+    if (tid == 0) {
+        float R = 0.f;
+        for (int t = 0; t < nt; ++t) R = __fadd_rn(R, sh_t[t]);
+        const float target = __fmul_rn(u, R);
+        float acc;
+        const int t = scan_pick(sh_t, nt, target, 0.f, &acc);
+        sh_i[0] = t;
+        sh_w[16] = target;
+        sh_w[17] = acc;
+    }
+    __syncthreads();
+    const int t = sh_i[0];
+    if (t < 0) return -1;  // uniform: every thread read the same value
+    sh_p[tid] = part[(t * 2 + slot) * kThreads + tid];
+    __syncthreads();
+    if (tid == 0) {
+        float acc;
+        sh_i[1] = scan_pick(sh_p, kThreads, sh_w[16], sh_w[17], &acc);
+        sh_w[18] = acc;
+    }
+    __syncthreads();
+    const int i = sh_i[1];
+    if (i < 0) return -1;
+    if (tid < 16) {
+        const int j = t * kTileElems + (tid >> 2) * 1024 + 4 * i + (tid & 3);
+        float wv = 0.f;
+        if (j < V) {
+            wv = w.p(__ldg(w.xt + j));
+            if (residual) wv = w.residual(wv, __ldg(w.xd + j));
+        }
+        sh_w[tid] = wv;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        float acc;
+        const int e = scan_pick(sh_w, 16, sh_w[16], sh_w[18], &acc);
+        sh_i[2] = e < 0 ? -1 : t * kTileElems + (e >> 2) * 1024 + 4 * i + (e & 3);
+    }
+    __syncthreads();
+    const int r = sh_i[2];
+    __syncthreads();  // the shared buffers may be reused by the next call
+    return r;
+}
+
+__global__ void __launch_bounds__(kThreads) pick_kernel(Rows R, const PickInfo* info, int nt, const float* part,
+                                                        const float* tsum, const float* us, int32_t* out_tokens) {
+    __shared__ float sh_t[kMaxTiles], sh_p[kThreads], sh_w[20];
+    __shared__ int sh_i[3];
+    const int b = blockIdx.x;
+    const PickInfo pi = info[b];
+    const Weight w = make_weight(R, pi, b);
+    const float* pb = part + int64_t(b) * nt * 2 * kThreads;
+    const float* tb = tsum + int64_t(b) * nt * 2;
+    const float u = us[b];
+    int tok = -1;
+    if (pi.rej < R.k) tok = pick_slot(w, true, R.V, nt, pb, tb, 0, u, sh_t, sh_p, sh_w, sh_i);
+    if (tok < 0) tok = pick_slot(w, false, R.V, nt, pb, tb, 1, u, sh_t, sh_p, sh_w, sh_i);
+    if (tok < 0) tok = 0;
+    if (threadIdx.x == 0) out_tokens[b * (R.k + 1) + pi.rej] = tok;
+}
+
+// Workspace carve-up (each part 256-byte aligned).
+struct Layout {
+    size_t tstats, info, part, tsum, total;
+};
+__host__ __device__ inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+inline Layout layout(int32_t batch, int32_t num_draft, int32_t vocab) {
+    const size_t nt = (size_t(vocab) + kTileElems - 1) / kTileElems;
+    const size_t rows = size_t(batch) * (2 * size_t(num_draft) + 1);
+    Layout L;
+    L.tstats = 0;
+    L.info = L.tstats + align256(rows * nt * sizeof(float2));
+    L.part = L.info + align256(size_t(batch) * sizeof(PickInfo));
+    L.tsum = L.part + align256(size_t(batch) * nt * 2 * kThreads * sizeof(float));
+    L.total = L.tsum + align256(size_t(batch) * nt * 2 * sizeof(float));
+    return L;
 }
 
 }  // namespace spec
 }  // namespace b200
 
 extern "C" size_t b200_spec_accept_workspace_size(int32_t batch, int32_t num_draft, int32_t vocab_size) {
-    (void)vocab_size;
-    if (batch < 0 || num_draft < 0) return 0;
-    const size_t rows = size_t(batch) * (2 * size_t(num_draft) + 1);
-    return ((rows * sizeof(float2)) + 255) & ~size_t(255);
+    if (batch < 0 || num_draft < 0 || vocab_size <= 0) return 0;
+    return b200::spec::layout(batch, num_draft, vocab_size).total;
 }
 
 extern "C" int32_t b200_spec_accept(int32_t* out_tokens, int32_t* out_num_tokens, const float* target_logits,
@@ -382,16 +439,23 @@ extern "C" int32_t b200_spec_accept(int32_t* out_tokens, int32_t* out_num_tokens
     if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 15))
         return fail(B200_ERR_WORKSPACE, "spec_accept: workspace needs %zu bytes (16-byte aligned)", need);
     Rows R{target_logits, draft_logits, temperatures, batch, num_draft, vocab_size};
-    float2* stats = static_cast<float2*>(workspace);
+    const Layout L = layout(batch, num_draft, vocab_size);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    float2* tstats = reinterpret_cast<float2*>(ws + L.tstats);
+    PickInfo* info = reinterpret_cast<PickInfo*>(ws + L.info);
+    float* part = reinterpret_cast<float*>(ws + L.part);
+    float* tsum = reinterpret_cast<float*>(ws + L.tsum);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    const int nrows = batch * (2 * num_draft + 1);
-    row_stats_kernel<<<nrows, kThreads, 0, s>>>(R, stats);
-    B200_CUDA_TRY(cudaGetLastError());
-    Decide d{R, stats, draft_tokens, uniform_accept, uniform_sample, out_tokens, out_num_tokens};
     const int nt = (vocab_size + kTileElems - 1) / kTileElems;
-    const int smem = nt * (kThreads + kThreads / 32) * int(sizeof(float));
-    ensure_smem_attr((const void*)decide_kernel, smem);
-    decide_kernel<<<batch, kThreads, smem, s>>>(d);
+    const int nrows = batch * (2 * num_draft + 1);
+    tile_stats_kernel<<<nrows * nt, kThreads, 0, s>>>(R, tstats, nt);
+    B200_CUDA_TRY(cudaGetLastError());
+    Decide d{R, tstats, draft_tokens, uniform_accept, uniform_sample, out_tokens, out_num_tokens, nt};
+    decide_kernel<<<batch, kDecideThreads, 0, s>>>(d, info);
+    B200_CUDA_TRY(cudaGetLastError());
+    weights_kernel<<<batch * nt, kThreads, 0, s>>>(R, info, nt, part, tsum);
+    B200_CUDA_TRY(cudaGetLastError());
+    pick_kernel<<<batch, kThreads, 0, s>>>(R, info, nt, part, tsum, uniform_sample, out_tokens);
     B200_CUDA_TRY(cudaGetLastError());
     return B200_OK;
 }
