@@ -2,18 +2,21 @@
 //
 // The reference engine has no speculative path; this op is new.  Its
 // arithmetic is defined in a fixed order with float32 rounding at every
-// step (__fmul_rn/__fadd_rn/__fdiv_rn, no contraction into FMA), so that a
-// CPU restatement reproduces accept/reject decisions and sampled tokens bit
-// for bit given the same uniforms:
-//   exp_c(x) = 2^n * P(f), y = x*log2(e), n = rint(y), f = y - n, P the
-//              degree-7 Taylor polynomial of 2^f in Horner form, 0 below y=-125;
+// step (__fmul_rn/__fadd_rn/__fmaf_rn/__frcp_rn, no implicit contraction),
+// so that a CPU restatement reproduces accept/reject decisions and sampled
+// tokens bit for bit given the same uniforms:
+//   exp_c(x), x <= 0: y = min(x*log2(e), 0), n = rint(y) through the magic
+//              constant 1.5*2^23, f = y - n, P(f) the degree-7 Taylor
+//              polynomial of 2^f by fused multiply-add Horner steps,
+//              exp_c = P * 2^n by an exponent-field add, 0 below y = -125;
 //   row sums: tiles of 4096; thread i of 256 adds its elements
 //              k*1024 + 4i + c (k outer, c inner), a warp xor-butterfly
 //              (16,8,4,2,1) combines 32 threads, 8 warp sums and then the
 //              tile sums are added left to right;
 //   normaliser: per tile M_t = tile max, S_t = tile sum of exp_c(x - M_t);
 //              M = max_t M_t, S = sum_t S_t * exp_c(M_t - M) (left to right);
-//              p_j = exp_c(x_j - M) / S; non-finite logits weigh 0;
+//              p_j = exp_c(x_j - M) * (1/S), the reciprocal rounded once;
+//              non-finite logits weigh 0;
 //   sampling: inverse CDF over tile sums, thread sums of the chosen tile,
 //              then the thread's 16 elements, each scanned left to right.
 //
@@ -40,15 +43,19 @@ constexpr float kLog2e = 0x1.715476p+0f;
 __device__ __constant__ float kExpCoef[8] = {0x1.0p+0f,      0x1.62e430p-1f,  0x1.ebfbe0p-3f, 0x1.c6b08ep-5f,
                                               0x1.3b2ab6p-7f, 0x1.5d87fep-10f, 0x1.430912p-13f, 0x1.ffcbfcp-17f};
 
+constexpr float kMagic = 12582912.f;  // 1.5 * 2^23: y + kMagic holds rint(y) in its low mantissa bits
+
 __device__ __forceinline__ float exp_c(float x) {
-    const float y = __fmul_rn(x, kLog2e);
-    const float n = rintf(y);
+    const float y = fminf(__fmul_rn(x, kLog2e), 0.f);
+    const float t = __fadd_rn(y, kMagic);
+    const float n = __fsub_rn(t, kMagic);
     const float f = __fsub_rn(y, n);
     float p = kExpCoef[7];
 #pragma unroll
-    for (int k = 6; k >= 0; --k) p = __fadd_rn(__fmul_rn(p, f), kExpCoef[k]);
-    const int ni = int(fminf(fmaxf(n, -126.f), 127.f));
-    const float r = __fmul_rn(p, __int_as_float((ni + 127) << 23));
+    for (int k = 6; k >= 0; --k) p = __fmaf_rn(p, f, kExpCoef[k]);
+    // P in [0.7, 1.42] times 2^n, n in [-125, 0]: add n to the exponent field
+    const uint32_t n_bits = __float_as_uint(t) - 0x4B400000u;
+    const float r = __uint_as_float(__float_as_uint(p) + (n_bits << 23));
     return y < -125.f ? 0.f : r;
 }
 
@@ -80,19 +87,24 @@ __device__ __forceinline__ float warp_butterfly(float v) {
 
 // One tile (4096 values) of a row as this thread's 16 values, in the fixed
 // order k = 0..3 (stride 1024), c = 0..3; values past V read as -inf.
+// SCALED divides by the temperature (chosen once per CTA, not per value).
+template <bool SCALED>
 __device__ __forceinline__ void load_tile(const float* x, int V, int t, float T, bool vec, float (&v)[16]) {
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         const int base = t * kTileElems + k * 1024 + 4 * int(threadIdx.x);
         if (vec && base + 3 < V) {
             const float4 f = __ldg(reinterpret_cast<const float4*>(x + base));
-            v[4 * k] = scaled(f.x, T);
-            v[4 * k + 1] = scaled(f.y, T);
-            v[4 * k + 2] = scaled(f.z, T);
-            v[4 * k + 3] = scaled(f.w, T);
+            v[4 * k] = SCALED ? __fdiv_rn(f.x, T) : f.x;
+            v[4 * k + 1] = SCALED ? __fdiv_rn(f.y, T) : f.y;
+            v[4 * k + 2] = SCALED ? __fdiv_rn(f.z, T) : f.z;
+            v[4 * k + 3] = SCALED ? __fdiv_rn(f.w, T) : f.w;
         } else {
 #pragma unroll
-            for (int c = 0; c < 4; ++c) v[4 * k + c] = base + c < V ? scaled(__ldg(x + base + c), T) : -INFINITY;
+            for (int c = 0; c < 4; ++c) {
+                const float l = base + c < V ? __ldg(x + base + c) : -INFINITY;
+                v[4 * k + c] = SCALED && base + c < V ? __fdiv_rn(l, T) : l;
+            }
         }
     }
 }
@@ -107,7 +119,10 @@ __global__ void __launch_bounds__(kThreads) tile_stats_kernel(Rows R, float2* ts
     const float T = R.temps ? R.temps[b] : 0.f;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     float v[16];
-    load_tile(x, R.V, t, T, (R.V & 3) == 0, v);
+    if (T > 0.f)
+        load_tile<true>(x, R.V, t, T, (R.V & 3) == 0, v);
+    else
+        load_tile<false>(x, R.V, t, T, (R.V & 3) == 0, v);
     float m = -INFINITY;
 #pragma unroll
     for (int e = 0; e < 16; ++e) m = fmaxf(m, v[e]);
@@ -180,12 +195,17 @@ struct PickInfo {
 };
 
 // Weight of token j for the sampling row: p, and the residual max(p - q, 0).
+// rt / rd are the once-rounded reciprocals of the rows' normalisers.
 struct Weight {
     const float *xt, *xd;
-    float T, Mt, St, Md, Sd;
-    __device__ __forceinline__ float p(float lt) const { return __fdiv_rn(exp_c(__fsub_rn(scaled(lt, T), Mt)), St); }
+    float T, Mt, rt, Md, rd;
+    template <bool SCALED = true>
+    __device__ __forceinline__ float p(float lt) const {
+        return __fmul_rn(exp_c(__fsub_rn(SCALED ? scaled(lt, T) : lt, Mt)), rt);
+    }
+    template <bool SCALED = true>
     __device__ __forceinline__ float residual(float pv, float ld) const {
-        const float q = __fdiv_rn(exp_c(__fsub_rn(scaled(ld, T), Md)), Sd);
+        const float q = __fmul_rn(exp_c(__fsub_rn(SCALED ? scaled(ld, T) : ld, Md)), rd);
         return fmaxf(__fsub_rn(pv, q), 0.f);
     }
 };
@@ -222,8 +242,8 @@ __global__ void __launch_bounds__(kDecideThreads) decide_kernel(Decide d, PickIn
             const float2 st = ms[r], sd = ms[k + 1 + r];
             const float* xt = R.tl + (int64_t(b) * (k + 1) + r) * V;
             const float* xd = R.dl + (int64_t(b) * k + r) * V;
-            const float p = __fdiv_rn(exp_c(__fsub_rn(scaled(xt[x], T), st.x)), st.y);
-            const float q = __fdiv_rn(exp_c(__fsub_rn(scaled(xd[x], T), sd.x)), sd.y);
+            const float p = __fmul_rn(exp_c(__fsub_rn(scaled(xt[x], T), st.x)), __frcp_rn(st.y));
+            const float q = __fmul_rn(exp_c(__fsub_rn(scaled(xd[x], T), sd.x)), __frcp_rn(sd.y));
             acc = q > 0.f ? (d.ua[b * k + r] < fminf(1.f, __fdiv_rn(p, q))) : (p > 0.f);
         }
         accept_s[r] = acc;
@@ -257,22 +277,19 @@ __device__ __forceinline__ Weight make_weight(const Rows& R, const PickInfo& pi,
     w.xt = R.tl + (int64_t(b) * (R.k + 1) + pi.rej) * R.V;
     w.xd = pi.rej < R.k ? R.dl + (int64_t(b) * R.k + pi.rej) * R.V : nullptr;
     w.Mt = pi.Mt;
-    w.St = pi.St;
+    w.rt = __frcp_rn(pi.St);
     w.Md = pi.Md;
-    w.Sd = pi.Sd;
+    w.rd = pi.rej < R.k ? __frcp_rn(pi.Sd) : 0.f;
     return w;
 }
 
 // One tile of one sequence's sampling row: thread partials and tile sums of
 // the residual (slot 0, when the sequence rejected a draft) and of p (slot 1).
 // part [B][nt][2][256], tsum [B][nt][2].
-__global__ void __launch_bounds__(kThreads) weights_kernel(Rows R, const PickInfo* info, int nt, float* part,
-                                                           float* tsum) {
-    __shared__ float wred[2][kThreads / 32];
-    const int b = blockIdx.x / nt, t = blockIdx.x - b * nt;
+template <bool SCALED>
+__device__ __forceinline__ void weights_tile(const Rows& R, const PickInfo& pi, const Weight& w, int b, int t, int nt,
+                                             float* part, float* tsum, float (&wred)[2][kThreads / 32]) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, V = R.V;
-    const PickInfo pi = info[b];
-    const Weight w = make_weight(R, pi, b);
     const bool res = pi.rej < R.k;
     const bool vec = (V & 3) == 0;
     float lt[16], ld[16];
@@ -300,9 +317,9 @@ __global__ void __launch_bounds__(kThreads) weights_kernel(Rows R, const PickInf
     for (int e = 0; e < 16; ++e) {
         const int j = t * kTileElems + (e >> 2) * 1024 + 4 * tid + (e & 3);
         if (j < V) {
-            const float pv = w.p(lt[e]);
+            const float pv = w.p<SCALED>(lt[e]);
             acc_p = __fadd_rn(acc_p, pv);
-            if (res) acc_r = __fadd_rn(acc_r, w.residual(pv, ld[e]));
+            if (res) acc_r = __fadd_rn(acc_r, w.residual<SCALED>(pv, ld[e]));
         }
     }
     float* pp = part + (int64_t(b) * nt + t) * 2 * kThreads;
@@ -319,6 +336,18 @@ __global__ void __launch_bounds__(kThreads) weights_kernel(Rows R, const PickInf
         for (int x = 0; x < kThreads / 32; ++x) st = __fadd_rn(st, wred[tid][x]);
         tsum[(int64_t(b) * nt + t) * 2 + tid] = st;
     }
+}
+
+__global__ void __launch_bounds__(kThreads) weights_kernel(Rows R, const PickInfo* info, int nt, float* part,
+                                                           float* tsum) {
+    __shared__ float wred[2][kThreads / 32];
+    const int b = blockIdx.x / nt, t = blockIdx.x - b * nt;
+    const PickInfo pi = info[b];
+    const Weight w = make_weight(R, pi, b);
+    if (w.T > 0.f)
+        weights_tile<true>(R, pi, w, b, t, nt, part, tsum, wred);
+    else
+        weights_tile<false>(R, pi, w, b, t, nt, part, tsum, wred);
 }
 
 // Inverse-CDF pick over one slot's partials (one CTA of kThreads per

@@ -14,9 +14,12 @@ with p = softmax(target_logits / T) and q = softmax(draft_logits / T).
 Every floating-point operation is defined in a fixed order with float32
 rounding, so that the CUDA kernel reproduces the decisions and the sampled
 tokens bit for bit given identical uniforms:
-  * exp_c: exp(x) = 2^n * P(f) with y = x*log2(e), n = rint(y), f = y - n,
-    P the degree-7 Taylor polynomial of 2^f (coefficients ln2^k / k!),
-    Horner with separate multiply and add, 0 below y = -125;
+  * exp_c (for x <= 0): y = min(x*log2(e), 0); n = rint(y) by the magic
+    constant 1.5*2^23 (t = y + c, n = t - c, round to nearest even);
+    f = y - n; P(f) = the degree-7 Taylor polynomial of 2^f (coefficients
+    ln2^k / k!) by Horner with fused multiply-add (one rounding per step);
+    exp_c = P * 2^n (exponent field add), 0 below y = -125;
+  * probabilities: p_j = exp_c(x_j - M) * r with r = 1 / S rounded once;
   * sums: the vocabulary is cut into tiles of 4096; in a tile, "thread" i
     (0..255) adds its 16 elements k*1024 + 4*i + c (k = 0..3 outer,
     c = 0..3 inner) left to right; the 32 thread sums of each warp are
@@ -25,7 +28,7 @@ tokens bit for bit given identical uniforms:
   * softmax normaliser of a row: per tile t, M_t = max of the tile and
     S_t = the tile sum of exp_c(x - M_t); then M = max_t M_t and
     S = sum_t S_t * exp_c(M_t - M) (left to right), so that a row is read
-    once; p_j = exp_c(x_j - M) / S;
+    once;
   * sampling: inverse CDF over the same hierarchy (tile sums, then thread
     sums, then the thread's 16 elements), each level scanned left to right
     with float32 running sums; a level where rounding leaves the target
@@ -42,19 +45,52 @@ LOG2E = f32(1.4426950408889634)
 EXP2_COEF = [f32(math.log(2.0) ** k / math.factorial(k)) for k in range(8)]
 
 
+def fma32(a, b, c):
+    """float32 a*b + c with a single rounding (round to nearest even), exactly.
+
+    a*b is exact in float64 (48-bit product).  hi = fl64(a*b + c) and the
+    TwoSum error lo give a*b + c = hi + lo exactly.  Rounding hi to float32
+    is correct unless hi sits exactly on a float32 midpoint (midpoints are
+    float64 numbers, so hi cannot straddle one); there the sign of lo breaks
+    the tie.
+    """
+    a = np.asarray(a, f32)
+    b = np.asarray(b, f32)
+    c = np.asarray(c, f32)
+    with np.errstate(invalid="ignore", over="ignore"):
+        s_ = a.astype(np.float64) * b.astype(np.float64)
+        c64 = c.astype(np.float64)
+        hi = s_ + c64
+        bb = hi - s_
+        lo = (s_ - (hi - bb)) + (c64 - bb)
+        r = hi.astype(f32)
+        r64 = r.astype(np.float64)
+        toward = np.where(hi > r64, np.float32(np.inf), np.float32(-np.inf)).astype(f32)
+        other = np.nextafter(r, toward)
+        mid = (r64 + other.astype(np.float64)) * 0.5
+        fix = (hi == mid) & (lo != 0) & np.isfinite(hi)
+        up = np.maximum(r, other)
+        down = np.minimum(r, other)
+        out = np.where(fix, np.where(lo > 0, up, down), r)
+    return out.astype(f32)
+
+
+MAGIC = f32(12582912.0)  # 1.5 * 2^23
+
+
 def exp_c(x):
-    """exp(x) for float32 x <= ~87 with the fixed operation order above."""
+    """exp(x) for float32 x <= 0 with the fixed operation order above."""
     x = np.asarray(x, dtype=f32)
-    y = (x * LOG2E).astype(f32)
-    n = np.rint(y).astype(f32)
+    y = np.minimum((x * LOG2E).astype(f32), f32(0.0))
+    t = (y + MAGIC).astype(f32)
+    n = (t - MAGIC).astype(f32)
     fr = (y - n).astype(f32)
     p = np.full_like(fr, EXP2_COEF[7])
     for c in EXP2_COEF[6::-1]:
-        p = (p * fr).astype(f32)
-        p = (p + c).astype(f32)
-    ni = np.clip(n, -126, 127).astype(np.int32)
-    scale = ((ni + 127).astype(np.uint32) << np.uint32(23)).view(f32)
-    r = (p * scale).astype(f32)
+        p = fma32(p, fr, c)
+    ni = np.where(y < f32(-125.0), 0, n).astype(np.int32)
+    bits = (p.view(np.int32) + (ni << np.int32(23))).astype(np.int32)
+    r = bits.view(f32)
     return np.where(y < f32(-125.0), f32(0.0), r).astype(f32)
 
 
@@ -156,8 +192,12 @@ def row_stats(x):
     return M, S
 
 
+def recip(S):
+    return (f32(1.0) / f32(S)).astype(f32) if np.ndim(S) else f32(f32(1.0) / f32(S))
+
+
 def probs(x, M, S):
-    return (exp_c((x - M).astype(f32)) / S).astype(f32)
+    return (exp_c((x - M).astype(f32)) * recip(S)).astype(f32)
 
 
 def spec_accept_ref(target_logits, draft_logits, draft_tokens, u_accept, u_sample,
@@ -181,8 +221,8 @@ def spec_accept_ref(target_logits, draft_logits, draft_tokens, u_accept, u_sampl
             xd = scaled_logits(dl[b, i], T)
             Mt, St = row_stats(xt)
             Md, Sd = row_stats(xd)
-            p = f32(exp_c(f32(xt[x] - Mt)) / St)
-            q = f32(exp_c(f32(xd[x] - Md)) / Sd)
+            p = f32(exp_c(f32(xt[x] - Mt)) * recip(St))
+            q = f32(exp_c(f32(xd[x] - Md)) * recip(Sd))
             if q > 0:
                 acc = f32(u_accept[b, i]) < min(f32(1.0), f32(p / q))
             else:

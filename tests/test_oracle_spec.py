@@ -13,6 +13,23 @@ def test_exp_c_accuracy():
     assert ss.exp_c(np.float32(-100.0)) == 0 and ss.exp_c(np.float32(0.0)) == 1.0
 
 
+def test_fma32_single_rounding():
+    """The oracle's fused multiply-add rounds a*b + c once, as the GPU's fma does."""
+    from fractions import Fraction
+    rng = np.random.default_rng(5)
+    n = 3000
+    a = rng.standard_normal(n).astype(np.float32)
+    b = rng.standard_normal(n).astype(np.float32)
+    c = (rng.standard_normal(n) * np.exp2(rng.integers(-40, 10, n))).astype(np.float32)
+    r = ss.fma32(a, b, c)
+    for i in range(n):
+        exact = Fraction(float(a[i])) * Fraction(float(b[i])) + Fraction(float(c[i]))
+        got = Fraction(float(r[i]))
+        for nb in (np.nextafter(r[i], np.float32(-np.inf)), np.nextafter(r[i], np.float32(np.inf))):
+            d_nb, d_got = abs(Fraction(float(nb)) - exact), abs(got - exact)
+            assert d_nb > d_got or (d_nb == d_got and not int(r[i].view(np.int32)) & 1), (a[i], b[i], c[i])
+
+
 def test_canonical_sum_close_to_exact():
     rng = np.random.default_rng(0)
     for V in (1, 4095, 4096, 4097, 151936):
