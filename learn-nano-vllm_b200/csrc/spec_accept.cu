@@ -6,8 +6,8 @@
 // so that a CPU restatement reproduces accept/reject decisions and sampled
 // tokens bit for bit given the same uniforms:
 //   exp_c(x), x <= 0: y = min(x*log2(e), 0), n = rint(y) through the magic
-//              constant 1.5*2^23, f = y - n, P(f) the degree-7 Taylor
-//              polynomial of 2^f by fused multiply-add Horner steps,
+//              constant 1.5*2^23, f = y - n, P(f) a degree-5 fit of 2^f
+//              (relative error 1.7e-7, P(0) = 1) by fused multiply-add steps,
 //              exp_c = P * 2^n by an exponent-field add, 0 below y = -125;
 //   row sums: tiles of 4096; thread i of 256 adds its elements
 //              k*1024 + 4i + c (k outer, c inner), a warp xor-butterfly
@@ -40,8 +40,10 @@ constexpr int kThreads = 256;
 constexpr int kTileElems = 4096;
 constexpr int kMaxTiles = 48;  // vocab <= 196608
 constexpr float kLog2e = 0x1.715476p+0f;
-__device__ __constant__ float kExpCoef[8] = {0x1.0p+0f,      0x1.62e430p-1f,  0x1.ebfbe0p-3f, 0x1.c6b08ep-5f,
-                                              0x1.3b2ab6p-7f, 0x1.5d87fep-10f, 0x1.430912p-13f, 0x1.ffcbfcp-17f};
+// 2^f on [-1/2, 1/2]: degree-5 relative-error fit with P(0) = 1 (max relative error 1.7e-7)
+constexpr int kExpDeg = 5;
+__device__ __constant__ float kExpCoef[kExpDeg + 1] = {0x1.0p+0f,       0x1.62e42ap-1f, 0x1.ebf9bcp-3f,
+                                                       0x1.c6b752p-5f,  0x1.3cea88p-7f, 0x1.5bba14p-10f};
 
 constexpr float kMagic = 12582912.f;  // 1.5 * 2^23: y + kMagic holds rint(y) in its low mantissa bits
 
@@ -50,9 +52,9 @@ __device__ __forceinline__ float exp_c(float x) {
     const float t = __fadd_rn(y, kMagic);
     const float n = __fsub_rn(t, kMagic);
     const float f = __fsub_rn(y, n);
-    float p = kExpCoef[7];
+    float p = kExpCoef[kExpDeg];
 #pragma unroll
-    for (int k = 6; k >= 0; --k) p = __fmaf_rn(p, f, kExpCoef[k]);
+    for (int k = kExpDeg - 1; k >= 0; --k) p = __fmaf_rn(p, f, kExpCoef[k]);
     // P in [0.7, 1.42] times 2^n, n in [-125, 0]: add n to the exponent field
     const uint32_t n_bits = __float_as_uint(t) - 0x4B400000u;
     const float r = __uint_as_float(__float_as_uint(p) + (n_bits << 23));

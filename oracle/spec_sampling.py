@@ -16,8 +16,9 @@ rounding, so that the CUDA kernel reproduces the decisions and the sampled
 tokens bit for bit given identical uniforms:
   * exp_c (for x <= 0): y = min(x*log2(e), 0); n = rint(y) by the magic
     constant 1.5*2^23 (t = y + c, n = t - c, round to nearest even);
-    f = y - n; P(f) = the degree-7 Taylor polynomial of 2^f (coefficients
-    ln2^k / k!) by Horner with fused multiply-add (one rounding per step);
+    f = y - n; P(f) = a degree-5 polynomial for 2^f on [-1/2, 1/2] (fitted
+    for relative error, 1.7e-7 at most, P(0) = 1; float32 coefficients
+    EXP2_COEF) by Horner with fused multiply-add (one rounding per step);
     exp_c = P * 2^n (exponent field add), 0 below y = -125;
   * probabilities: p_j = exp_c(x_j - M) * r with r = 1 / S rounded once;
   * sums: the vocabulary is cut into tiles of 4096; in a tile, "thread" i
@@ -25,7 +26,8 @@ tokens bit for bit given identical uniforms:
     c = 0..3 inner) left to right; the 32 thread sums of each warp are
     combined by an xor butterfly (16, 8, 4, 2, 1); the 8 warp sums are
     added left to right; tile sums are added left to right;
-  * softmax normaliser of a row: per tile t, M_t = max of the tile and
+  * softmax normaliser of a row: per tile t, M_t = max of the tile (NaN
+    values ignored, as fmaxf does) and
     S_t = the tile sum of exp_c(x - M_t); then M = max_t M_t and
     S = sum_t S_t * exp_c(M_t - M) (left to right), so that a row is read
     once;
@@ -34,15 +36,15 @@ tokens bit for bit given identical uniforms:
     with float32 running sums; a level where rounding leaves the target
     above the running sum falls back to its last positive entry.
 """
-import math
 import numpy as np
 
 f32 = np.float32
 TILE = 4096
 THREADS = 256
 LOG2E = f32(1.4426950408889634)
-# 2^f = sum_k (f ln2)^k / k!  ->  coefficients ln2^k / k!, rounded to float32
-EXP2_COEF = [f32(math.log(2.0) ** k / math.factorial(k)) for k in range(8)]
+# 2^f ~ sum_k c_k f^k on [-1/2, 1/2]: relative-error fit with c_0 = 1 (float32)
+EXP2_COEF = [f32(float.fromhex(h)) for h in ("0x1.0p+0", "0x1.62e42ap-1", "0x1.ebf9bcp-3", "0x1.c6b752p-5",
+                                               "0x1.3cea88p-7", "0x1.5bba14p-10")]
 
 
 def fma32(a, b, c):
@@ -85,8 +87,8 @@ def exp_c(x):
     t = (y + MAGIC).astype(f32)
     n = (t - MAGIC).astype(f32)
     fr = (y - n).astype(f32)
-    p = np.full_like(fr, EXP2_COEF[7])
-    for c in EXP2_COEF[6::-1]:
+    p = np.full_like(fr, EXP2_COEF[-1])
+    for c in EXP2_COEF[-2::-1]:
         p = fma32(p, fr, c)
     ni = np.where(y < f32(-125.0), 0, n).astype(np.int32)
     bits = (p.view(np.int32) + (ni << np.int32(23))).astype(np.int32)
@@ -180,7 +182,7 @@ def row_stats(x):
     pad = np.full(T * TILE, -np.inf, f32)
     pad[:V] = x
     tiles = pad.reshape(T, TILE)
-    Mt = tiles.max(axis=1).astype(f32)
+    Mt = np.fmax.reduce(tiles, axis=1).astype(f32)
     with np.errstate(invalid="ignore"):
         e = exp_c((tiles - Mt[:, None]).astype(f32))
     e = np.where(np.isfinite(tiles), e, f32(0.0)).astype(f32)
