@@ -53,7 +53,7 @@ def parse():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--workload", choices=["decode", "prefill", "verify", "engine"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "prefill", "verify", "engine", "qknorm"], default="decode",
                     help="decode = config 5 (the bench line); prefill = config 3; verify = config 4; "
                          "engine = config 2 through nano-vLLM's own engine (1 GPU)")
     ap.add_argument("--engine-attn", choices=["b200", "flash_attn"], default="b200",
@@ -410,6 +410,87 @@ def run_verify(args, pkg, torch, dev):
         "clocks": clk.summary()}), flush=True)
 
 
+def _time_graph(torch, stream, fn, steps, warmup, calls=20):
+    """Device time per call with `calls` calls captured in one CUDA graph (no host launch
+    overhead in the timed region, as in nano-vLLM's decode graphs)."""
+    for _ in range(max(warmup, 3)):
+        fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(calls):
+            fn()
+    ms = _time(torch, stream, g.replay, max(steps // calls, 5), 3) / calls
+    del g
+    return ms
+
+
+def run_qknorm(args, pkg, torch, dev):
+    """Fused q/k RMSNorm + RoPE + KV scatter (the Qwen3 attention layer's epilogue of
+    the QKV projection) on config 3's prefill tokens (0.6B shape) and on config 5's
+    decode batch (8B shape), beside the reference's own unfused modules (RMSNorm and
+    RotaryEmbedding under torch.compile, Triton store_kvcache) from baseline/_ref."""
+    d, base, max_pos, eps = 128, 1e6, 40960, 1e-6
+    inv_freq = 1.0 / (base ** (torch.arange(0, d, 2, dtype=torch.float) / d))
+    freqs = torch.einsum("i,j -> ij", torch.arange(max_pos, dtype=torch.float), inv_freq)
+    cs = torch.cat((freqs.cos(), freqs.sin()), dim=-1).to(dev)
+    ref = None
+    try:
+        sys.path.insert(0, os.path.join(ROOT, "baseline", "_ref"))
+        from nanovllm.layers.layernorm import RMSNorm
+        from nanovllm.layers.rotary_embedding import RotaryEmbedding
+        from nanovllm.layers.attention import store_kvcache as ref_store
+        ref = (RMSNorm, RotaryEmbedding, ref_store)
+    except Exception as e:  # the reference arm is optional here
+        ref_err = f"{type(e).__name__}: {e}"
+    hbm = measured_peak()
+    results = {}
+    rng = np.random.default_rng(0)
+    for name, T, hq, hkv in (("config3 prefill tokens, Qwen3-0.6B", 18715, 16, 8),
+                             ("config5 decode batch, Qwen3-8B", 512, 32, 8)):
+        g = torch.Generator(device=dev).manual_seed(5)
+        qkv = (torch.randn(T, (hq + 2 * hkv) * d, generator=g, device=dev) * 1.5).to(torch.bfloat16)
+        positions = torch.from_numpy(rng.integers(0, 4096, T).astype(np.int64)).to(dev)
+        wq = (1 + 0.1 * torch.randn(d, generator=g, device=dev)).to(torch.bfloat16)
+        wk = (1 + 0.1 * torch.randn(d, generator=g, device=dev)).to(torch.bfloat16)
+        nslots = T + 4096
+        kc = torch.zeros(nslots // 256 + 1, 256, hkv, d, dtype=torch.bfloat16, device=dev)
+        vc = torch.zeros_like(kc)
+        slots = torch.from_numpy(rng.permutation(nslots)[:T].astype(np.int32)).to(dev)
+        fused = lambda: pkg.qk_norm_rope_store(qkv, positions, hq, hkv, wq, wk, eps, cs, kc, vc, slots)
+        stream = torch.cuda.current_stream(dev)
+        timer = _time if T > 4096 else _time_graph  # small calls: graph replay, as the engine's decode does
+        with ClockSampler(dev.index or 0) as clk:
+            ms = timer(torch, stream, fused, args.steps, args.warmup)
+        nbytes = T * ((hq + 2 * hkv) * d * 2 + hq * d * 2 + hkv * d * 2 + 2 * hkv * d * 2 + d * 4 + 12)
+        r = {"tokens": T, "heads": f"{hq}/{hkv}", "us": round(ms * 1e3, 2),
+             "timing": "event loop" if T > 4096 else "CUDA graph of 20 calls, per call",
+             "GBps": round(nbytes / (ms / 1e3) / 1e9, 1), "frac_hbm": round(nbytes / (ms / 1e3) / 1e9 / hbm[0], 4),
+             "bytes_per_call": nbytes, "gpu_launches_per_call": 1, "clocks": clk.summary()}
+        if ref is not None:
+            RMSNorm, RotaryEmbedding, ref_store = ref
+            qn, kn = RMSNorm(d, eps).to(dev, torch.bfloat16), RMSNorm(d, eps).to(dev, torch.bfloat16)
+            rope = RotaryEmbedding(d, d, max_pos, base).to(dev)
+
+            def unfused():
+                q, k, v = qkv.split([hq * d, hkv * d, hkv * d], dim=-1)
+                q = qn(q.view(-1, hq, d))
+                k = kn(k.view(-1, hkv, d))
+                q, k = rope(positions, q, k)
+                ref_store(k, v.view(-1, hkv, d), kc, vc, slots)
+            rms = timer(torch, stream, unfused, max(args.steps // 4, 20), max(args.warmup, 5))
+            r["reference_unfused_us"] = round(rms * 1e3, 2)
+            r["speedup_vs_reference"] = round(rms / ms, 2)
+        else:
+            r["reference_unfused"] = f"unavailable: {ref_err}"
+        results[name] = r
+    print(json.dumps({"metric": "fused q/k norm + RoPE + KV scatter GB/s", "unit": "GB/s",
+                      "value": results["config3 prefill tokens, Qwen3-0.6B"]["GBps"], "n_gpus": 1,
+                      "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "dtype": "bf16",
+                      "data": "synthetic (seeded)", "peak_GBps": hbm[0], "peak_kind": hbm[1],
+                      "cases": results}), flush=True)
+
+
 QWEN3 = {
     "qwen3-0.6b": dict(hidden_size=1024, intermediate_size=3072, num_hidden_layers=28, num_attention_heads=16,
                        num_key_value_heads=8, tie_word_embeddings=True),
@@ -534,8 +615,8 @@ def main():
         run_engine(args, pkg)
         return
     if args.workload != "decode":
-        assert world == 1, "the prefill / verify workloads run on one GPU"
-        (run_prefill if args.workload == "prefill" else run_verify)(args, pkg, torch, dev)
+        assert world == 1, "the prefill / verify / qknorm workloads run on one GPU"
+        {"prefill": run_prefill, "verify": run_verify, "qknorm": run_qknorm}[args.workload](args, pkg, torch, dev)
         return
     if world > 1:
         from datetime import timedelta

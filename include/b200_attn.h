@@ -72,6 +72,36 @@ B200_API int32_t b200_store_kvcache(const void* key, int64_t key_stride,
                            int64_t num_slots, int32_t elem_bytes, void* stream);
 
 /*
+ * Fused q/k RMSNorm + rotary embedding + KV-cache scatter for Qwen3 layers.
+ * Replaces, in one pass over the fused QKV projection output `qkv`
+ * ([num_tokens, (Hq + 2 Hkv) * D], token stride qkv_stride):
+ *     q = q_norm(q); k = k_norm(k)           nanovllm/models/qwen3.py:82-84
+ *                                            (RMSNorm, nanovllm/layers/layernorm.py:16-26)
+ *     q, k = rotary_emb(positions, q, k)     qwen3.py:85 (layers/rotary_embedding.py:6-14, 37-48)
+ *     store_kvcache(k, v, k_cache, v_cache, slot_mapping)   layers/attention.py:60-63
+ * Rounding follows the reference's eager order: RMSNorm in fp32, rounded to
+ * the model dtype, times the weight (rounded); RoPE in fp32 on the rounded
+ * normalised values, rounded.  cos_sin is the model's cos_sin_cache,
+ * [max_position, D] fp32 with cos in the first D/2 columns and sin in the
+ * rest; positions (int64) are clamped to [0, max_position).
+ * Outputs: q_out [num_tokens, Hq, D] (token stride q_out_stride); k_out
+ * [num_tokens, Hkv, D] or NULL; the rotated k and the unchanged v rows go to
+ * k_cache / v_cache [num_slots, Hkv, D] at slot_mapping[t] (NULL caches: no
+ * store; slots of -1 or outside the cache are skipped).  All rows 8-byte
+ * aligned (cos_sin 16-byte); D == 128; dtype bf16 or fp16.
+ */
+B200_API int32_t b200_qk_norm_rope_store(void* q_out, int64_t q_out_stride,
+                                void* k_out, int64_t k_out_stride,
+                                const void* qkv, int64_t qkv_stride,
+                                const int64_t* positions,
+                                const void* q_weight, const void* k_weight, float eps,
+                                const float* cos_sin, int32_t max_position,
+                                void* k_cache, void* v_cache,
+                                const int32_t* slot_mapping, int64_t num_slots,
+                                int32_t num_tokens, int32_t num_heads, int32_t num_kv_heads,
+                                int32_t head_dim, int32_t dtype, void* stream);
+
+/*
  * Paged multi-query attention over the KV cache: decode (query_len == 1)
  * and speculative verify (query_len == k+1).  Replaces the decode call of
  * nanovllm/layers/attention.py:71-74:

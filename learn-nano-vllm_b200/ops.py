@@ -229,3 +229,53 @@ def spec_accept(target_logits, draft_logits, draft_tokens, uniform_accept, unifo
                                 B, k, V, workspace.data_ptr(), workspace.numel(), _stream(target_logits))
     check(rc, "spec_accept")
     return tokens, num
+
+
+# ------------------------------------------- fused q/k norm + RoPE + KV scatter
+def qk_norm_rope_store(qkv: torch.Tensor, positions: torch.Tensor, num_heads: int, num_kv_heads: int,
+                       q_weight: torch.Tensor, k_weight: torch.Tensor, eps: float, cos_sin_cache: torch.Tensor,
+                       k_cache: torch.Tensor | None = None, v_cache: torch.Tensor | None = None,
+                       slot_mapping: torch.Tensor | None = None, return_k: bool = True):
+    """One pass over the QKV projection output of a Qwen3 attention layer.
+
+    Equivalent to (nanovllm/models/qwen3.py:79-85 and layers/attention.py:60-63)
+        q, k, v = qkv.split([Hq*D, Hkv*D, Hkv*D], -1)
+        q = q_norm(q.view(-1, Hq, D)); k = k_norm(k.view(-1, Hkv, D))
+        q, k = rotary_emb(positions, q, k)
+        store_kvcache(k, v.view(-1, Hkv, D), k_cache, v_cache, slot_mapping)
+    Returns (q [T, Hq, D], k [T, Hkv, D] or None, v view [T, Hkv, D]).
+    cos_sin_cache is the rotary module's buffer ([max_position, 1, D] or
+    [max_position, D], fp32, cos | sin).  Empty caches (numel 0, the
+    reference's "no cache yet") skip the store.
+    """
+    assert qkv.dim() == 2 and qkv.stride(-1) == 1, "qkv must be [T, (Hq+2Hkv)*D] with contiguous rows"
+    T = qkv.shape[0]
+    D = q_weight.numel()
+    assert qkv.shape[1] == (num_heads + 2 * num_kv_heads) * D, "qkv width does not match the head counts"
+    assert k_weight.numel() == D and q_weight.is_contiguous() and k_weight.is_contiguous()
+    assert q_weight.dtype == k_weight.dtype == qkv.dtype, "norm weights must have the model dtype"
+    assert qkv.dtype in _DTYPES, f"unsupported dtype {qkv.dtype}"
+    assert positions.dtype == torch.int64 and positions.numel() == T and positions.is_contiguous()
+    cs = cos_sin_cache.reshape(cos_sin_cache.shape[0], -1)
+    assert cs.dtype == torch.float32 and cs.shape[1] == D and cs.is_contiguous(), "cos_sin_cache must be fp32 [P, D]"
+    has_cache = k_cache is not None and v_cache is not None and k_cache.numel() > 0 and v_cache.numel() > 0
+    tensors = [qkv, positions, q_weight, k_weight, cs]
+    if has_cache:
+        assert slot_mapping is not None and slot_mapping.dtype == torch.int32 and slot_mapping.numel() == T
+        assert slot_mapping.is_contiguous() and k_cache.is_contiguous() and v_cache.is_contiguous()
+        assert k_cache.dtype == v_cache.dtype == qkv.dtype, "cache dtype differs from qkv"
+        assert k_cache.numel() % (num_kv_heads * D) == 0
+        tensors += [k_cache, v_cache, slot_mapping]
+    _require_cuda(*tensors)
+    q = torch.empty((T, num_heads, D), dtype=qkv.dtype, device=qkv.device)
+    k = torch.empty((T, num_kv_heads, D), dtype=qkv.dtype, device=qkv.device) if return_k else None
+    num_slots = k_cache.numel() // (num_kv_heads * D) if has_cache else 0
+    rc = lib().b200_qk_norm_rope_store(
+        q.data_ptr(), q.stride(0), k.data_ptr() if k is not None else None, k.stride(0) if k is not None else 0,
+        qkv.data_ptr(), qkv.stride(0), positions.data_ptr(), q_weight.data_ptr(), k_weight.data_ptr(), float(eps),
+        cs.data_ptr(), cs.shape[0], k_cache.data_ptr() if has_cache else None,
+        v_cache.data_ptr() if has_cache else None, slot_mapping.data_ptr() if has_cache else None, num_slots, T,
+        num_heads, num_kv_heads, D, _DTYPES[qkv.dtype], _stream(qkv))
+    check(rc, "qk_norm_rope_store")
+    v = qkv[:, (num_heads + num_kv_heads) * D:].view(T, num_kv_heads, D)
+    return q, k, v
