@@ -56,7 +56,7 @@ def parse():
     ap.add_argument("--workload", choices=["decode", "prefill", "verify", "engine", "qknorm"], default="decode",
                     help="decode = config 5 (the bench line); prefill = config 3; verify = config 4; "
                          "engine = config 2 through nano-vLLM's own engine (1 GPU)")
-    ap.add_argument("--engine-attn", choices=["b200", "flash_attn"], default="b200",
+    ap.add_argument("--engine-attn", choices=["b200", "b200-fused", "flash_attn"], default="b200",
                     help="engine workload: this package's Attention, or the reference's stock flash-attn path")
     ap.add_argument("--engine-model", choices=["qwen3-0.6b", "qwen3-8b"], default="qwen3-0.6b")
     ap.add_argument("--engine-requests", type=int, default=256)
@@ -551,8 +551,8 @@ def run_engine(args, pkg):
     import nanovllm.engine.model_runner as mr
     le.AutoTokenizer = _IdTokenizer
     mr.load_model = _random_init
-    if args.engine_attn == "b200":
-        pkg.install()
+    if args.engine_attn in ("b200", "b200-fused"):
+        pkg.install(fuse_qk_epilogue=args.engine_attn == "b200-fused")
     from nanovllm import LLM, SamplingParams
     path = _qwen3_config_dir(args.engine_model)
     t_init = time.perf_counter()

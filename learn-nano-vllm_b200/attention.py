@@ -14,7 +14,7 @@ import torch
 from torch import nn
 
 from . import context as _ctx
-from .ops import flash_attn_varlen_func, flash_attn_with_kvcache, store_kvcache
+from .ops import flash_attn_varlen_func, flash_attn_with_kvcache, qk_norm_rope_store, store_kvcache
 
 # Where forward() reads the metadata from; integrate.install() rebinds it to
 # the reference's nanovllm.utils.context.get_context.
@@ -41,6 +41,26 @@ class Attention(nn.Module):
         cache_bound = self.k_cache.numel() > 0 and self.v_cache.numel() > 0
         if cache_bound:
             store_kvcache(k, v, self.k_cache, self.v_cache, ctx.slot_mapping)
+        return self._attend(ctx, q, k, v)
+
+    def forward_fused(self, qkv: torch.Tensor, positions: torch.Tensor, q_norm, k_norm,
+                      rotary_emb) -> torch.Tensor:
+        """q/k RMSNorm, RoPE and the cache store in one kernel, then attention.
+
+        Same result as Qwen3Attention.forward's q_norm / k_norm / rotary_emb
+        (nanovllm/models/qwen3.py:82-85) followed by forward(q, k, v); qkv is the
+        fused projection output [T, (Hq + 2 Hkv) * D].
+        """
+        ctx = _get_context()
+        cache_bound = self.k_cache.numel() > 0 and self.v_cache.numel() > 0
+        need_k = ctx.is_prefill and (ctx.block_tables is None or not cache_bound)
+        q, k, v = qk_norm_rope_store(qkv, positions, self.num_heads, self.num_kv_heads, q_norm.weight,
+                                     k_norm.weight, q_norm.eps, rotary_emb.cos_sin_cache,
+                                     self.k_cache if cache_bound else None, self.v_cache if cache_bound else None,
+                                     ctx.slot_mapping if cache_bound else None, return_k=need_k)
+        return self._attend(ctx, q, k, v)
+
+    def _attend(self, ctx, q, k, v):
         if not ctx.is_prefill:
             return flash_attn_with_kvcache(q.unsqueeze(1), self.k_cache, self.v_cache,
                                            cache_seqlens=ctx.context_lens, block_table=ctx.block_tables,

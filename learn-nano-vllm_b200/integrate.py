@@ -10,12 +10,33 @@ builds its model.
 """
 import importlib
 
+import torch
+
 from . import attention as _attention
 from .ops import store_kvcache
 
 
-def install():
-    """Patch the importable `nanovllm` package; returns the patched modules."""
+def _fused_qwen3_attention_forward(self, positions, hidden_states):
+    """Qwen3Attention.forward (nanovllm/models/qwen3.py:72-88) with q/k norm, RoPE and the
+    KV-cache store fused into one kernel (Attention.forward_fused)."""
+    if (self.qkv_bias or self.head_dim != 128 or not isinstance(self.attn, _attention.Attention)
+            or hidden_states.dtype not in (torch.bfloat16, torch.float16)):
+        return _ORIGINAL_FORWARD[0](self, positions, hidden_states)
+    qkv = self.qkv_proj(hidden_states)
+    o = self.attn.forward_fused(qkv, positions, self.q_norm, self.k_norm, self.rotary_emb)
+    return self.o_proj(o.flatten(1, -1))
+
+
+_ORIGINAL_FORWARD = []
+
+
+def install(fuse_qk_epilogue: bool = False):
+    """Patch the importable `nanovllm` package; returns the patched modules.
+
+    With fuse_qk_epilogue, Qwen3Attention.forward also runs q/k RMSNorm, RoPE and
+    the KV-cache store as one kernel (ops.qk_norm_rope_store) instead of the
+    reference's separate RMSNorm / RotaryEmbedding modules and store.
+    """
     ctx_mod = importlib.import_module("nanovllm.utils.context")
     attn_mod = importlib.import_module("nanovllm.layers.attention")
     qwen3 = importlib.import_module("nanovllm.models.qwen3")
@@ -23,6 +44,9 @@ def install():
     attn_mod.Attention = _attention.Attention
     attn_mod.store_kvcache = store_kvcache
     qwen3.Attention = _attention.Attention
+    if not _ORIGINAL_FORWARD:
+        _ORIGINAL_FORWARD.append(qwen3.Qwen3Attention.forward)
+    qwen3.Qwen3Attention.forward = _fused_qwen3_attention_forward if fuse_qk_epilogue else _ORIGINAL_FORWARD[0]
     return attn_mod, qwen3
 
 
