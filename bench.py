@@ -53,10 +53,10 @@ def parse():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--workload", choices=["decode", "prefill", "verify", "engine", "qknorm"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "prefill", "verify", "engine", "qknorm", "sample"], default="decode",
                     help="decode = config 5 (the bench line); prefill = config 3; verify = config 4; "
                          "engine = config 2 through nano-vLLM's own engine (1 GPU)")
-    ap.add_argument("--engine-attn", choices=["b200", "b200-fused", "flash_attn"], default="b200",
+    ap.add_argument("--engine-attn", choices=["b200", "b200-fused", "b200-fused-all", "flash_attn"], default="b200",
                     help="engine workload: this package's Attention, or the reference's stock flash-attn path")
     ap.add_argument("--engine-model", choices=["qwen3-0.6b", "qwen3-8b"], default="qwen3-0.6b")
     ap.add_argument("--engine-requests", type=int, default=256)
@@ -491,6 +491,41 @@ def run_qknorm(args, pkg, torch, dev):
                       "cases": results}), flush=True)
 
 
+def run_sample(args, pkg, torch, dev):
+    """Fused sampler on a decode batch's logits (B = 512, Qwen3 vocab 151,936, bf16 as the
+    LM head returns them), beside the reference's own Sampler (torch.compile) from baseline/_ref."""
+    B, V = 512, 151936
+    g = torch.Generator(device=dev).manual_seed(6)
+    logits = (torch.randn(B, V, generator=g, device=dev) * 2).to(torch.bfloat16)
+    temps = torch.empty(B, device=dev).uniform_(0.5, 1.5, generator=g)
+    step = [0]
+
+    def fused():
+        step[0] += 1
+        return pkg.sample(logits, temps, seed=1, offset=step[0])
+    stream = torch.cuda.current_stream(dev)
+    with ClockSampler(dev.index or 0) as clk:
+        ms = _time(torch, stream, fused, args.steps, args.warmup)
+    hbm = measured_peak()
+    nbytes = B * V * 2 + B * 12
+    line = {"metric": "fused sampler GB/s (logits read once)", "value": round(nbytes / (ms / 1e3) / 1e9, 1),
+            "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "dtype": "bf16 logits, fp32 math", "data": "synthetic logits N(0, 4), T U[0.5, 1.5]",
+            "config": {"workload": "decode batch 512 x vocab 151936"}, "us_per_call": round(ms * 1e3, 2),
+            "frac_hbm": round(nbytes / (ms / 1e3) / 1e9 / hbm[0], 4), "peak_kind": hbm[1],
+            "gpu_launches_per_call": 2, "clocks": clk.summary()}
+    try:
+        sys.path.insert(0, os.path.join(ROOT, "baseline", "_ref"))
+        from nanovllm.layers.sampler import Sampler
+        ref = Sampler()
+        rms = _time(torch, stream, lambda: ref(logits, temps), max(args.steps // 4, 20), max(args.warmup, 5))
+        line["reference_sampler_us"] = round(rms * 1e3, 2)
+        line["speedup_vs_reference"] = round(rms / ms, 2)
+    except Exception as e:
+        line["reference_sampler"] = f"unavailable: {type(e).__name__}: {e}"
+    print(json.dumps(line), flush=True)
+
+
 QWEN3 = {
     "qwen3-0.6b": dict(hidden_size=1024, intermediate_size=3072, num_hidden_layers=28, num_attention_heads=16,
                        num_key_value_heads=8, tie_word_embeddings=True),
@@ -551,8 +586,8 @@ def run_engine(args, pkg):
     import nanovllm.engine.model_runner as mr
     le.AutoTokenizer = _IdTokenizer
     mr.load_model = _random_init
-    if args.engine_attn in ("b200", "b200-fused"):
-        pkg.install(fuse_qk_epilogue=args.engine_attn == "b200-fused")
+    if args.engine_attn.startswith("b200"):
+        pkg.install(fuse_qk_epilogue=args.engine_attn != "b200", fuse_sampler=args.engine_attn == "b200-fused-all")
     from nanovllm import LLM, SamplingParams
     path = _qwen3_config_dir(args.engine_model)
     t_init = time.perf_counter()
@@ -616,7 +651,8 @@ def main():
         return
     if args.workload != "decode":
         assert world == 1, "the prefill / verify / qknorm workloads run on one GPU"
-        {"prefill": run_prefill, "verify": run_verify, "qknorm": run_qknorm}[args.workload](args, pkg, torch, dev)
+        {"prefill": run_prefill, "verify": run_verify, "qknorm": run_qknorm,
+         "sample": run_sample}[args.workload](args, pkg, torch, dev)
         return
     if world > 1:
         from datetime import timedelta

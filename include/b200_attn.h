@@ -102,6 +102,29 @@ B200_API int32_t b200_qk_norm_rope_store(void* q_out, int64_t q_out_stride,
                                 int32_t head_dim, int32_t dtype, void* stream);
 
 /*
+ * Fused sampler.  Replaces nanovllm/layers/sampler.py:7-12
+ *     token[b] = argmax_j softmax(logits[b] / T[b])_j / clamp_min(E[b, j], 1e-10)
+ * computed as argmax_j (logits[b, j] / T[b] - log E[b, j]) (the softmax only
+ * rescales a row), one pass over the logits.  E is the caller's noise
+ * [batch, V] fp32 (row stride noise_stride; e.g. the reference's own
+ * exponential_ draw), or, with noise == NULL, Exp(1) samples -log(U) with U
+ * from Philox-4x32-10: counter (j / 4, b, offset_lo, offset_hi), key
+ * (seed_lo, seed_hi), output word j % 4, U = ((bits >> 8) + 0.5) * 2^-24 —
+ * the same (seed, offset) gives the same tokens on any grid.  Ties go to the
+ * smallest index (torch.argmax).
+ * logits [batch, V] (row stride row_stride, dtype bf16 / fp16 / fp32);
+ * temperatures [batch] fp32 (> 0, as SamplingParams asserts);
+ * out_tokens [batch] int64 (torch.argmax's dtype).
+ * workspace: b200_sample_workspace_size(batch) bytes, 16-byte aligned.
+ */
+B200_API size_t b200_sample_workspace_size(int32_t batch);
+
+B200_API int32_t b200_sample(int64_t* out_tokens, const void* logits, int64_t row_stride, int32_t dtype,
+                    const float* temperatures, int32_t batch, int32_t vocab_size,
+                    const float* noise, int64_t noise_stride, uint64_t seed, uint64_t offset,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Paged multi-query attention over the KV cache: decode (query_len == 1)
  * and speculative verify (query_len == k+1).  Replaces the decode call of
  * nanovllm/layers/attention.py:71-74:

@@ -11,6 +11,7 @@ Public API
   paged_attention           the same decode kernel with explicit arguments
   spec_accept               speculative acceptance sampling
   qk_norm_rope_store        fused q/k RMSNorm + RoPE + KV-cache scatter (Qwen3 layer epilogue)
+  sample                    fused temperature + exponential-race sampler
   install                   patch nano-vLLM to use this package's Attention
   context                   mirror of nanovllm.utils.context
 """
@@ -19,8 +20,8 @@ from ._native import B200Error, lib
 from .attention import Attention
 from .integrate import install
 from .ops import (flash_attn_varlen_func, flash_attn_with_kvcache, paged_attention, paged_workspace,
-                  qk_norm_rope_store, spec_accept, store_kvcache, workspace_error)
+                  qk_norm_rope_store, sample, spec_accept, store_kvcache, workspace_error)
 
 __all__ = ["Attention", "B200Error", "context", "flash_attn_varlen_func", "flash_attn_with_kvcache", "install",
-           "lib", "paged_attention", "paged_workspace", "qk_norm_rope_store", "spec_accept", "store_kvcache",
-           "workspace_error"]
+           "lib", "paged_attention", "paged_workspace", "qk_norm_rope_store", "sample", "spec_accept",
+           "store_kvcache", "workspace_error"]

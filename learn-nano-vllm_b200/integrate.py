@@ -28,14 +28,31 @@ def _fused_qwen3_attention_forward(self, positions, hidden_states):
 
 
 _ORIGINAL_FORWARD = []
+_ORIGINAL_SAMPLER = []
 
 
-def install(fuse_qk_epilogue: bool = False):
+class _FusedSamplerState:
+    """Seed and per-call offset of the fused sampler's counter-based noise."""
+    seed = 0
+    offset = 0
+
+
+def _fused_sampler_forward(self, logits, temperatures):
+    """Sampler.forward (nanovllm/layers/sampler.py:7-12) as one fused kernel: the same
+    exponential race, with its Exp(1) noise drawn in-kernel (fresh offset per call)."""
+    from .ops import sample
+    _FusedSamplerState.offset += 1
+    return sample(logits, temperatures, seed=_FusedSamplerState.seed, offset=_FusedSamplerState.offset)
+
+
+def install(fuse_qk_epilogue: bool = False, fuse_sampler: bool = False):
     """Patch the importable `nanovllm` package; returns the patched modules.
 
     With fuse_qk_epilogue, Qwen3Attention.forward also runs q/k RMSNorm, RoPE and
     the KV-cache store as one kernel (ops.qk_norm_rope_store) instead of the
-    reference's separate RMSNorm / RotaryEmbedding modules and store.
+    reference's separate RMSNorm / RotaryEmbedding modules and store.  With
+    fuse_sampler, Sampler.forward becomes the one-pass fused sampler (ops.sample;
+    its noise stream is seeded from torch.initial_seed()).
     """
     ctx_mod = importlib.import_module("nanovllm.utils.context")
     attn_mod = importlib.import_module("nanovllm.layers.attention")
@@ -47,6 +64,12 @@ def install(fuse_qk_epilogue: bool = False):
     if not _ORIGINAL_FORWARD:
         _ORIGINAL_FORWARD.append(qwen3.Qwen3Attention.forward)
     qwen3.Qwen3Attention.forward = _fused_qwen3_attention_forward if fuse_qk_epilogue else _ORIGINAL_FORWARD[0]
+    sampler_mod = importlib.import_module("nanovllm.layers.sampler")
+    if not _ORIGINAL_SAMPLER:
+        _ORIGINAL_SAMPLER.append(sampler_mod.Sampler.forward)
+    if fuse_sampler:
+        _FusedSamplerState.seed = torch.initial_seed() & (2 ** 64 - 1)
+    sampler_mod.Sampler.forward = _fused_sampler_forward if fuse_sampler else _ORIGINAL_SAMPLER[0]
     return attn_mod, qwen3
 
 

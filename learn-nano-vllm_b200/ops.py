@@ -279,3 +279,42 @@ def qk_norm_rope_store(qkv: torch.Tensor, positions: torch.Tensor, num_heads: in
     check(rc, "qk_norm_rope_store")
     v = qkv[:, (num_heads + num_kv_heads) * D:].view(T, num_kv_heads, D)
     return q, k, v
+
+
+# ------------------------------------------------------------------ sampler
+_DTYPES_ALL = {torch.bfloat16: _native.B200_BF16, torch.float16: _native.B200_F16, torch.float32: _native.B200_F32}
+_sample_ws: dict[int, torch.Tensor] = {}
+
+
+def sample(logits: torch.Tensor, temperatures: torch.Tensor, seed: int = 0, offset: int = 0,
+           noise: torch.Tensor | None = None) -> torch.Tensor:
+    """Fused temperature + exponential-race sampling (nanovllm/layers/sampler.py:7-12).
+
+    Returns int64 tokens [B].  With `noise` ([B, V] fp32, Exp(1) draws) the result is
+    argmax(softmax(logits / T) / clamp_min(noise, 1e-10)) as in the reference; without it
+    the noise comes from the counter-based generator keyed by (seed, offset) — advance
+    `offset` every step to draw fresh noise.
+    """
+    assert logits.dim() == 2 and logits.stride(-1) == 1, "logits must be [B, V] with contiguous rows"
+    assert logits.dtype in _DTYPES_ALL, f"unsupported dtype {logits.dtype}"
+    B, V = logits.shape
+    assert temperatures.dtype == torch.float32 and temperatures.numel() == B and temperatures.is_contiguous()
+    tensors = [logits, temperatures]
+    if noise is not None:
+        assert noise.dtype == torch.float32 and noise.shape == (B, V) and noise.stride(-1) == 1
+        tensors.append(noise)
+    _require_cuda(*tensors)
+    need = lib().b200_sample_workspace_size(B)
+    dev = logits.device.index if logits.device.index is not None else torch.cuda.current_device()
+    ws = _sample_ws.get(dev)
+    if ws is None or ws.numel() < need:
+        assert not torch.cuda.is_current_stream_capturing(), "call sample() once eagerly before graph capture"
+        ws = torch.empty(max(need, 256), dtype=torch.uint8, device=logits.device)
+        _sample_ws[dev] = ws
+    out = torch.empty(B, dtype=torch.int64, device=logits.device)
+    rc = lib().b200_sample(out.data_ptr(), logits.data_ptr(), logits.stride(0), _DTYPES_ALL[logits.dtype],
+                           temperatures.data_ptr(), B, V, noise.data_ptr() if noise is not None else None,
+                           noise.stride(0) if noise is not None else 0, seed & (2 ** 64 - 1),
+                           offset & (2 ** 64 - 1), ws.data_ptr(), ws.numel(), _stream(logits))
+    check(rc, "sample")
+    return out
