@@ -61,6 +61,9 @@ def parse():
     ap.add_argument("--engine-model", choices=["qwen3-0.6b", "qwen3-8b"], default="qwen3-0.6b")
     ap.add_argument("--engine-requests", type=int, default=256)
     ap.add_argument("--gpu-mem", type=float, default=0.5, help="engine KV-cache share of GPU memory")
+    ap.add_argument("--rank-shape", type=int, default=0,
+                    help="decode on one GPU with rank 0's head shard of an N-way tensor-parallel job "
+                         "(per-rank kernel efficiency at TP N without N GPUs)")
     ap.add_argument("--batch", type=int, default=BATCH,
                     help="sequences in the batch (profiling runs use a smaller batch; the bench line uses 512)")
     return ap.parse_args()
@@ -660,7 +663,9 @@ def main():
 
     ctx = workload(args.batch)
     BATCH = len(ctx)
-    hq, hkv = HQ_TOTAL // world, HKV_TOTAL // world
+    shard = args.rank_shape if (args.rank_shape and world == 1) else world
+    assert HKV_TOTAL % shard == 0, f"{shard} does not divide {HKV_TOTAL} kv heads"
+    hq, hkv = HQ_TOTAL // shard, HKV_TOTAL // shard
     nblk = (ctx + BLOCK - 1) // BLOCK
     nb = int(nblk.sum())
     width = int(nblk.max())
@@ -787,7 +792,8 @@ def main():
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5),
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
                 "data": "synthetic (seeded random bf16 KV cache, q, new k/v)",
-                "config": config_dict(world, ctx),
+                "config": dict(config_dict(world, ctx), **({"rank_shape": f"one GPU running rank 0's shard of tp{shard}"}
+                                                        if shard != world else {})),
                 "e2e": {"value": round((dec_b + store_b) * world / (e2e_ms / 1e3) / 1e9, 2), "unit": "GB/s",
                         "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                         "ms_per_step": round(e2e_ms, 5), "api": "Attention.forward (decode), pinned host buffers"},
