@@ -51,7 +51,7 @@ constexpr int kCounterSlots = 65536;
 constexpr int kCtrlWords = 64;               // [0] next item, [1] finished CTAs, [2] error word
 constexpr size_t kFixedBytes = kCtrlWords * 4 + size_t(kCounterSlots) * 4;
 constexpr int kWaves = 4;
-constexpr int kChunkMaxTiles = 16;           // at most 2048 tokens per item
+constexpr int kChunkMaxTiles = 32;           // at most 4096 tokens per item
 constexpr int kSplitBarrier = 1;             // named barrier of the consumer warps
 constexpr int kRemBits = 12;                 // packed offsets: full-chunk offset << 12 | remainder offset
 
