@@ -61,6 +61,24 @@ __device__ __forceinline__ float exp_c(float x) {
     return y < -125.f ? 0.f : r;
 }
 
+// exp_c of two values with packed f32x2 arithmetic: each lane of mul / add /
+// fma .rn.f32x2 rounds exactly as the scalar instruction, so the results are
+// bit-identical to exp_c and the issue slots are about halved.
+__device__ __forceinline__ float2 exp_c2(float2 x) {
+    float2 y = fmul2(x, make_float2(kLog2e, kLog2e));
+    y.x = fminf(y.x, 0.f);
+    y.y = fminf(y.y, 0.f);
+    const float2 t = fadd2(y, make_float2(kMagic, kMagic));
+    const float2 n = fadd2(t, make_float2(-kMagic, -kMagic));
+    const float2 f = fadd2(y, make_float2(-n.x, -n.y));
+    float2 p = make_float2(kExpCoef[kExpDeg], kExpCoef[kExpDeg]);
+#pragma unroll
+    for (int k = kExpDeg - 1; k >= 0; --k) p = ffma2(p, f, make_float2(kExpCoef[k], kExpCoef[k]));
+    const float rx = __uint_as_float(__float_as_uint(p.x) + ((__float_as_uint(t.x) - 0x4B400000u) << 23));
+    const float ry = __uint_as_float(__float_as_uint(p.y) + ((__float_as_uint(t.y) - 0x4B400000u) << 23));
+    return make_float2(y.x < -125.f ? 0.f : rx, y.y < -125.f ? 0.f : ry);
+}
+
 struct Rows {
     const float* tl;   // [B, k+1, V]
     const float* dl;   // [B, k, V]
@@ -136,10 +154,17 @@ __global__ void __launch_bounds__(kThreads) tile_stats_kernel(Rows R, float2* ts
 #pragma unroll
     for (int w = 1; w < kThreads / 32; ++w) Mt = fmaxf(Mt, wred[w]);
     __syncthreads();
+    float ex[16];
+#pragma unroll
+    for (int e = 0; e < 16; e += 2) {
+        const float2 r = exp_c2(fadd2(make_float2(v[e], v[e + 1]), make_float2(-Mt, -Mt)));
+        ex[e] = r.x;
+        ex[e + 1] = r.y;
+    }
     float acc = 0.f;
 #pragma unroll
     for (int e = 0; e < 16; ++e)
-        if (isfinite(v[e])) acc = __fadd_rn(acc, exp_c(__fsub_rn(v[e], Mt)));
+        if (isfinite(v[e])) acc = __fadd_rn(acc, ex[e]);
     const float ws = warp_butterfly(acc);
     if (lane == 0) wred[warp] = ws;
     __syncthreads();
@@ -314,14 +339,31 @@ __device__ __forceinline__ void weights_tile(const Rows& R, const PickInfo& pi, 
             }
         }
     }
+    // p and q for pairs of values (packed f32x2, bit-identical to the scalar path), then the
+    // fixed-order sums
+    float pv[16], rv[16];
+#pragma unroll
+    for (int e = 0; e < 16; e += 2) {
+        float2 a = make_float2(lt[e], lt[e + 1]);
+        if (SCALED) a = make_float2(scaled(a.x, w.T), scaled(a.y, w.T));
+        const float2 pp2 = fmul2(exp_c2(fadd2(a, make_float2(-w.Mt, -w.Mt))), make_float2(w.rt, w.rt));
+        pv[e] = pp2.x;
+        pv[e + 1] = pp2.y;
+        if (res) {
+            float2 c = make_float2(ld[e], ld[e + 1]);
+            if (SCALED) c = make_float2(scaled(c.x, w.T), scaled(c.y, w.T));
+            const float2 q2 = fmul2(exp_c2(fadd2(c, make_float2(-w.Md, -w.Md))), make_float2(w.rd, w.rd));
+            rv[e] = fmaxf(__fsub_rn(pp2.x, q2.x), 0.f);
+            rv[e + 1] = fmaxf(__fsub_rn(pp2.y, q2.y), 0.f);
+        }
+    }
     float acc_r = 0.f, acc_p = 0.f;
 #pragma unroll
     for (int e = 0; e < 16; ++e) {
         const int j = t * kTileElems + (e >> 2) * 1024 + 4 * tid + (e & 3);
         if (j < V) {
-            const float pv = w.p<SCALED>(lt[e]);
-            acc_p = __fadd_rn(acc_p, pv);
-            if (res) acc_r = __fadd_rn(acc_r, w.residual<SCALED>(pv, ld[e]));
+            acc_p = __fadd_rn(acc_p, pv[e]);
+            if (res) acc_r = __fadd_rn(acc_r, rv[e]);
         }
     }
     float* pp = part + (int64_t(b) * nt + t) * 2 * kThreads;
