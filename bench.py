@@ -60,6 +60,7 @@ def parse():
                     help="engine workload: this package's Attention, or the reference's stock flash-attn path")
     ap.add_argument("--engine-model", choices=["qwen3-0.6b", "qwen3-8b"], default="qwen3-0.6b")
     ap.add_argument("--engine-requests", type=int, default=256)
+    ap.add_argument("--engine-tp", type=int, default=1, help="engine workload: tensor_parallel_size")
     ap.add_argument("--gpu-mem", type=float, default=0.5, help="engine KV-cache share of GPU memory")
     ap.add_argument("--rank-shape", type=int, default=0,
                     help="decode on one GPU with rank 0's head shard of an N-way tensor-parallel job "
@@ -577,6 +578,18 @@ def _random_init(model, path):
                 prm.normal_(0.0, 0.02, generator=g)
 
 
+def _engine_worker_setup():
+    """Run in every engine process (spawned ranks too): the stand-in weight loader and
+    tokenizer, and the reference checkout on sys.path."""
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if ref not in sys.path:
+        sys.path.insert(0, ref)
+    import nanovllm.engine.llm_engine as le
+    import nanovllm.engine.model_runner as mr
+    le.AutoTokenizer = _IdTokenizer
+    mr.load_model = _random_init
+
+
 def run_engine(args, pkg):
     """Config 2 through nano-vLLM's own LLM engine (scheduler, block manager,
     prefix cache, CUDA-graph decode): 256 requests, prompt and output lengths
@@ -584,17 +597,22 @@ def run_engine(args, pkg):
     ignore_eos; output tokens / wall time of generate() as in the reference
     bench.py:21-27.  Weights are random (no checkpoint is available)."""
     import torch
-    sys.path.insert(0, os.path.join(ROOT, "baseline", "_ref"))
-    import nanovllm.engine.llm_engine as le
-    import nanovllm.engine.model_runner as mr
-    le.AutoTokenizer = _IdTokenizer
-    mr.load_model = _random_init
+    _engine_worker_setup()
+    tp = args.engine_tp
     if args.engine_attn.startswith("b200"):
-        pkg.install(fuse_qk_epilogue=args.engine_attn != "b200", fuse_sampler=args.engine_attn == "b200-fused-all")
+        pkg.install(fuse_qk_epilogue=args.engine_attn != "b200", fuse_sampler=args.engine_attn == "b200-fused-all",
+                    workers=tp > 1, worker_setup=("bench:_engine_worker_setup",))
+    elif tp > 1:
+        # stock path: the spawned ranks still need the stand-in loader and tokenizer
+        import functools
+        import nanovllm.engine.llm_engine as le
+        import __graft_entry__ as entry
+        le.ModelRunner = functools.partial(entry.nanovllm_worker_stock, setup=("bench:_engine_worker_setup",))
     from nanovllm import LLM, SamplingParams
     path = _qwen3_config_dir(args.engine_model)
     t_init = time.perf_counter()
-    llm = LLM(path, enforce_eager=False, max_model_len=4096, gpu_memory_utilization=args.gpu_mem)
+    llm = LLM(path, enforce_eager=False, max_model_len=4096, gpu_memory_utilization=args.gpu_mem,
+              tensor_parallel_size=tp)
     t_init = time.perf_counter() - t_init
     rng = np.random.default_rng(0)
     n = args.engine_requests
@@ -612,10 +630,11 @@ def run_engine(args, pkg):
     assert all(len(o["token_ids"]) == sp.max_tokens for o, sp in zip(out, sps))
     print(json.dumps({
         "metric": "e2e output tokens/s (nano-vLLM engine, config 2)", "value": round(total / t, 1), "unit": "tok/s",
-        "n_gpus": 1, "higher_is_better": True, "dtype": "bf16", "data": "synthetic prompts, random-init weights",
+        "n_gpus": tp, "higher_is_better": True, "dtype": "bf16", "data": "synthetic prompts, random-init weights",
         "attention": args.engine_attn, "vs_baseline": round(total / t / 1434.13, 3),
         "config": {"workload": f"config2: {args.engine_model}, {n} requests, in/out U[100,1024], T=0.6, ignore_eos",
                    "output_tokens": total, "seconds": round(t, 3), "engine_init_s": round(t_init, 1),
+                   "tensor_parallel_size": tp,
                    "gpu_memory_utilization": args.gpu_mem},
         "clocks": clk.summary()}), flush=True)
 

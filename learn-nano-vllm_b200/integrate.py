@@ -45,14 +45,18 @@ def _fused_sampler_forward(self, logits, temperatures):
     return sample(logits, temperatures, seed=_FusedSamplerState.seed, offset=_FusedSamplerState.offset)
 
 
-def install(fuse_qk_epilogue: bool = False, fuse_sampler: bool = False):
+def install(fuse_qk_epilogue: bool = False, fuse_sampler: bool = False, workers: bool = False,
+            worker_setup: tuple = ()):
     """Patch the importable `nanovllm` package; returns the patched modules.
 
     With fuse_qk_epilogue, Qwen3Attention.forward also runs q/k RMSNorm, RoPE and
     the KV-cache store as one kernel (ops.qk_norm_rope_store) instead of the
     reference's separate RMSNorm / RotaryEmbedding modules and store.  With
     fuse_sampler, Sampler.forward becomes the one-pass fused sampler (ops.sample;
-    its noise stream is seeded from torch.initial_seed()).
+    its noise stream is seeded from torch.initial_seed()).  With workers, the
+    engine's tensor-parallel ranks (spawned processes, nanovllm/engine/llm_engine.py:24-30)
+    run install() with the same options before building their ModelRunner;
+    worker_setup lists "module:function" hooks they run first.
     """
     ctx_mod = importlib.import_module("nanovllm.utils.context")
     attn_mod = importlib.import_module("nanovllm.layers.attention")
@@ -70,6 +74,16 @@ def install(fuse_qk_epilogue: bool = False, fuse_sampler: bool = False):
     if fuse_sampler:
         _FusedSamplerState.seed = torch.initial_seed() & (2 ** 64 - 1)
     sampler_mod.Sampler.forward = _fused_sampler_forward if fuse_sampler else _ORIGINAL_SAMPLER[0]
+    engine_mod = importlib.import_module("nanovllm.engine.llm_engine")
+    runner_mod = importlib.import_module("nanovllm.engine.model_runner")
+    if workers:
+        import functools
+        entry = importlib.import_module("__graft_entry__")
+        opts = {"setup": list(worker_setup),
+                "install": {"fuse_qk_epilogue": fuse_qk_epilogue, "fuse_sampler": fuse_sampler}}
+        engine_mod.ModelRunner = functools.partial(entry.nanovllm_worker, options=opts)
+    else:
+        engine_mod.ModelRunner = runner_mod.ModelRunner
     return attn_mod, qwen3
 
 
