@@ -125,6 +125,26 @@ B200_API int32_t b200_sample(int64_t* out_tokens, const void* logits, int64_t ro
                     void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Decode-step metadata on the device.  Replaces the per-sequence host loops
+ * of nanovllm/engine/model_runner.py:167-193 (prepare_decode,
+ * prepare_block_tables, prepare_sample).  `packed` is a device int32 buffer
+ * (one host-to-device copy per step): [batch] lengths, [batch] last tokens,
+ * [batch] temperatures (fp32 bits), [batch + 1] offsets into `flat`, then
+ * `flat` = every block id of the batch, sequence after sequence.  Writes
+ *   input_ids[b] = last token, positions[b] = len - 1 (int64);
+ *   context_lens[b] = len, slot_mapping[b] = block_table[-1] * block_size +
+ *   (len - (num_blocks - 1) * block_size) - 1 (int32);
+ *   block_tables[b, j] = block_table[j] or -1 past the sequence's blocks,
+ *   [batch, max_blocks] int32 (max_blocks = the batch's longest table);
+ *   temperatures[b] (fp32).
+ * The host must give offsets that stay inside `flat` (the kernel trusts them).
+ */
+B200_API int32_t b200_decode_metadata(const int32_t* packed, int32_t batch, int32_t max_blocks,
+                             int32_t block_size, int64_t* input_ids, int64_t* positions,
+                             int32_t* slot_mapping, int32_t* context_lens, int32_t* block_tables,
+                             float* temperatures, void* stream);
+
+/*
  * Paged multi-query attention over the KV cache: decode (query_len == 1)
  * and speculative verify (query_len == k+1).  Replaces the decode call of
  * nanovllm/layers/attention.py:71-74:

@@ -29,6 +29,30 @@ def _fused_qwen3_attention_forward(self, positions, hidden_states):
 
 _ORIGINAL_FORWARD = []
 _ORIGINAL_SAMPLER = []
+_ORIGINAL_PREPARE = []
+
+
+def _device_prepare_decode(self, seqs):
+    """ModelRunner.prepare_decode (nanovllm/engine/model_runner.py:167-187) with the metadata
+    expanded on the device from one packed copy (decode_meta.DecodeMetadata)."""
+    from nanovllm.utils.context import set_context
+    from .decode_meta import DecodeMetadata
+    meta = self.__dict__.get("_b200_meta")
+    if meta is None:
+        meta = self._b200_meta = DecodeMetadata()
+    input_ids, positions, slot_mapping, context_lens, block_tables, temps = meta.build(seqs, self.block_size)
+    set_context(False, slot_mapping=slot_mapping, context_lens=context_lens, block_tables=block_tables)
+    self._b200_temps = (seqs, temps)
+    return input_ids, positions
+
+
+def _device_prepare_sample(self, seqs):
+    """ModelRunner.prepare_sample (model_runner.py:189-193): the temperatures of a decode batch
+    come with its device metadata; other batches use the reference's code."""
+    cached = self.__dict__.get("_b200_temps")
+    if cached is not None and cached[0] is seqs:
+        return cached[1]
+    return _ORIGINAL_PREPARE[1](self, seqs)
 
 
 class _FusedSamplerState:
@@ -46,14 +70,16 @@ def _fused_sampler_forward(self, logits, temperatures):
 
 
 def install(fuse_qk_epilogue: bool = False, fuse_sampler: bool = False, workers: bool = False,
-            worker_setup: tuple = ()):
+            worker_setup: tuple = (), device_metadata: bool = False):
     """Patch the importable `nanovllm` package; returns the patched modules.
 
     With fuse_qk_epilogue, Qwen3Attention.forward also runs q/k RMSNorm, RoPE and
     the KV-cache store as one kernel (ops.qk_norm_rope_store) instead of the
     reference's separate RMSNorm / RotaryEmbedding modules and store.  With
     fuse_sampler, Sampler.forward becomes the one-pass fused sampler (ops.sample;
-    its noise stream is seeded from torch.initial_seed()).  With workers, the
+    its noise stream is seeded from torch.initial_seed()).  With device_metadata,
+    ModelRunner.prepare_decode / prepare_sample build the decode step's tensors on
+    the device from one packed host-to-device copy (decode_meta).  With workers, the
     engine's tensor-parallel ranks (spawned processes, nanovllm/engine/llm_engine.py:24-30)
     run install() with the same options before building their ModelRunner;
     worker_setup lists "module:function" hooks they run first.
@@ -76,11 +102,16 @@ def install(fuse_qk_epilogue: bool = False, fuse_sampler: bool = False, workers:
     sampler_mod.Sampler.forward = _fused_sampler_forward if fuse_sampler else _ORIGINAL_SAMPLER[0]
     engine_mod = importlib.import_module("nanovllm.engine.llm_engine")
     runner_mod = importlib.import_module("nanovllm.engine.model_runner")
+    if not _ORIGINAL_PREPARE:
+        _ORIGINAL_PREPARE.extend([runner_mod.ModelRunner.prepare_decode, runner_mod.ModelRunner.prepare_sample])
+    runner_mod.ModelRunner.prepare_decode = _device_prepare_decode if device_metadata else _ORIGINAL_PREPARE[0]
+    runner_mod.ModelRunner.prepare_sample = _device_prepare_sample if device_metadata else _ORIGINAL_PREPARE[1]
     if workers:
         import functools
         entry = importlib.import_module("__graft_entry__")
         opts = {"setup": list(worker_setup),
-                "install": {"fuse_qk_epilogue": fuse_qk_epilogue, "fuse_sampler": fuse_sampler}}
+                "install": {"fuse_qk_epilogue": fuse_qk_epilogue, "fuse_sampler": fuse_sampler,
+                            "device_metadata": device_metadata}}
         engine_mod.ModelRunner = functools.partial(entry.nanovllm_worker, options=opts)
     else:
         engine_mod.ModelRunner = runner_mod.ModelRunner

@@ -1,0 +1,27 @@
+"""Decode-step metadata oracle (test infrastructure only).
+
+Restates nanovllm/engine/model_runner.py:123-127 (prepare_block_tables), :167-187
+(prepare_decode) and :189-193 (prepare_sample) for sequences given as
+(length, last_token, temperature, block_table list):
+  input_ids = last tokens; positions = len - 1; context_lens = len;
+  slot_mapping = block_table[-1] * block_size + last_block_num_tokens - 1 with
+  last_block_num_tokens = len - (len(block_table) - 1) * block_size
+  (nanovllm/engine/sequence.py); block_tables padded with -1 to the longest table.
+"""
+import numpy as np
+
+
+def decode_metadata_ref(seqs, block_size):
+    """seqs: list of (length, last_token, temperature, block_table)."""
+    lens = np.array([s[0] for s in seqs], np.int64)
+    toks = np.array([s[1] for s in seqs], np.int64)
+    temps = np.array([s[2] for s in seqs], np.float32)
+    tables = [list(s[3]) for s in seqs]
+    W = max(len(t) for t in tables)
+    bt = np.full((len(seqs), W), -1, np.int32)
+    slots = np.empty(len(seqs), np.int32)
+    for b, t in enumerate(tables):
+        bt[b, :len(t)] = t
+        last_n = lens[b] - (len(t) - 1) * block_size
+        slots[b] = t[-1] * block_size + last_n - 1
+    return toks, lens - 1, slots, lens.astype(np.int32), bt, temps
