@@ -53,7 +53,7 @@ def parse():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--workload", choices=["decode", "prefill", "verify", "engine", "qknorm", "sample"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "prefill", "verify", "engine", "qknorm", "sample", "oproj"], default="decode",
                     help="decode = config 5 (the bench line); prefill = config 3; verify = config 4; "
                          "engine = config 2 through nano-vLLM's own engine (1 GPU)")
     ap.add_argument("--engine-attn", choices=["b200", "b200-fused", "b200-fused-all", "b200-full", "flash_attn"], default="b200",
@@ -495,6 +495,64 @@ def run_qknorm(args, pkg, torch, dev):
                       "cases": results}), flush=True)
 
 
+def run_oproj(args, pkg, torch, dev, world, rank):
+    """Qwen3-8B attention output projection, row-parallel over the ranks (K = 4096 / world,
+    N = 4096), for a decode batch: the fused GEMM + all-reduce kernel against the reference's
+    path, F.linear (cuBLAS) then dist.all_reduce (NCCL).  Device time, max over ranks."""
+    import torch.distributed as dist
+    from datetime import timedelta
+    if not dist.is_initialized():
+        if world == 1:
+            os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+            os.environ.setdefault("MASTER_PORT", "29531")
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev, rank=rank,
+                                world_size=world)
+    hidden, k_total = 4096, 4096
+    K = k_total // world
+    results = {}
+    op = pkg.OprojAllReduce(dist.group.WORLD, max_tokens=512, hidden=hidden)
+    g = torch.Generator(device=dev).manual_seed(7 + rank)
+    w = (torch.randn(hidden, K, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    stream = torch.cuda.current_stream(dev)
+    for M in (512, 64):
+        a = torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16)
+
+        def fused():
+            op(a, w)
+
+        def reference():
+            y = torch.nn.functional.linear(a, w)
+            dist.all_reduce(y)
+        times = {}
+        for name, fn in (("fused", fused), ("reference", reference)):
+            for _ in range(max(args.warmup, 3)):
+                fn()
+            torch.cuda.synchronize()
+            dist.barrier(device_ids=[dev.index])
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(args.steps):
+                fn()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            t = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            times[name] = t.item() * 1e3
+        flops = 2.0 * M * hidden * k_total
+        results[f"M={M}"] = {"fused_us": round(times["fused"], 2), "reference_us": round(times["reference"], 2),
+                             "speedup": round(times["reference"] / times["fused"], 2),
+                             "fused_TFLOPs_total": round(flops / (times["fused"] * 1e-6) / 1e12, 1),
+                             "nvlink_bytes_in_per_rank": (world - 1) * M * hidden * 2}
+    assert op.error() == 0
+    if rank == 0:
+        print(json.dumps({"metric": "o_proj GEMM + all-reduce us per call (device, max over ranks)",
+                          "unit": "us", "higher_is_better": False, "n_gpus": world, "steps": args.steps,
+                          "warmup": args.warmup, "dtype": "bf16", "data": "synthetic",
+                          "config": {"workload": f"Qwen3-8B o_proj, hidden 4096, tp{world}"},
+                          "value": results["M=512"]["fused_us"], "cases": results}), flush=True)
+    dist.destroy_process_group()
+
+
 def run_sample(args, pkg, torch, dev):
     """Fused sampler on a decode batch's logits (B = 512, Qwen3 vocab 151,936, bf16 as the
     LM head returns them), beside the reference's own Sampler (torch.compile) from baseline/_ref."""
@@ -671,6 +729,9 @@ def main():
     if args.workload == "engine":
         assert world == 1, "the engine workload runs on one GPU"
         run_engine(args, pkg)
+        return
+    if args.workload == "oproj":
+        run_oproj(args, pkg, torch, dev, world, rank)
         return
     if args.workload != "decode":
         assert world == 1, "the prefill / verify / qknorm workloads run on one GPU"

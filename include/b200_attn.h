@@ -145,6 +145,32 @@ B200_API int32_t b200_decode_metadata(const int32_t* packed, int32_t batch, int3
                              float* temperatures, void* stream);
 
 /*
+ * Row-parallel output projection fused with its all-reduce over peer memory.
+ * Replaces RowParallelLinear.forward of the attention output projection
+ * (nanovllm/layers/linear.py:152-156, called at nanovllm/models/qwen3.py:87):
+ *     y = F.linear(a, w)   (a [M, K] this rank's shard, w [N, K]; bf16)
+ *     dist.all_reduce(y)
+ * One launch per rank: tcgen05 GEMM tiles of y_r (rounded to bf16) go to this
+ * rank's slot buffer and are announced with release flags; then every tile is
+ * summed over the ranks' slots (plain loads over NVLink, fp32, rank order, so
+ * all ranks get the same bits) into out [M, N] (row stride ldo).
+ * slots[r] / flags[r]: device arrays of every rank's buffers, mapped into this
+ * process (e.g. CUDA symmetric memory): slots [2][slot_rows][N] bf16, flags
+ * uint32 [max_tiles + 2] zeroed once before the first call.  epoch: 1, 2, 3,
+ * ... the same sequence on every rank (one call per epoch).  N % 256 == 0,
+ * K % 64 == 0, M <= slot_rows; a, w 16-byte aligned with strides that are
+ * multiples of 8 elements.  Bounded waits set the error word read by
+ * b200_oproj_allreduce_error (results of that call undefined).
+ */
+B200_API int32_t b200_oproj_allreduce(void* out, int64_t ldo, const void* a, int64_t lda,
+                             const void* w, int64_t ldw, int32_t M, int32_t N, int32_t K,
+                             void* const* slots, int32_t slot_rows,
+                             uint32_t* const* flags, int32_t max_tiles,
+                             int32_t rank, int32_t world, uint32_t epoch, void* stream);
+
+B200_API int32_t b200_oproj_allreduce_error(void* stream, int32_t* flag);
+
+/*
  * Paged multi-query attention over the KV cache: decode (query_len == 1)
  * and speculative verify (query_len == k+1).  Replaces the decode call of
  * nanovllm/layers/attention.py:71-74:

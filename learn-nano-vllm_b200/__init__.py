@@ -13,6 +13,7 @@ Public API
   qk_norm_rope_store        fused q/k RMSNorm + RoPE + KV-cache scatter (Qwen3 layer epilogue)
   sample                    fused temperature + exponential-race sampler
   DecodeMetadata            decode-step metadata built on the device
+  OprojAllReduce            tensor-parallel o_proj GEMM fused with its all-reduce over peer memory
   install                   patch nano-vLLM to use this package's Attention
   context                   mirror of nanovllm.utils.context
 """
@@ -20,10 +21,11 @@ from . import context, ops
 from ._native import B200Error, lib
 from .attention import Attention
 from .decode_meta import DecodeMetadata
+from .oproj import OprojAllReduce
 from .integrate import install
 from .ops import (flash_attn_varlen_func, flash_attn_with_kvcache, paged_attention, paged_workspace,
                   qk_norm_rope_store, sample, spec_accept, store_kvcache, workspace_error)
 
-__all__ = ["Attention", "B200Error", "DecodeMetadata", "context", "flash_attn_varlen_func", "flash_attn_with_kvcache", "install",
+__all__ = ["Attention", "B200Error", "DecodeMetadata", "OprojAllReduce", "context", "flash_attn_varlen_func", "flash_attn_with_kvcache", "install",
            "lib", "paged_attention", "paged_workspace", "qk_norm_rope_store", "sample", "spec_accept",
            "store_kvcache", "workspace_error"]

@@ -1,0 +1,61 @@
+"""Child process of tests/test_oproj_gpu.py: one rank of the fused o_proj + all-reduce.
+
+Usage: python tests/oproj_worker.py RANK WORLD PORT   (GPU = RANK).  Exits non-zero on a
+mismatch; prints one JSON line per rank.
+"""
+import json
+import os
+import sys
+from datetime import timedelta
+
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+
+def main():
+    rank, world, port = int(sys.argv[1]), int(sys.argv[2]), int(sys.argv[3])
+    import __graft_entry__
+    pkg = __graft_entry__.load_package()
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60), device_id=dev)
+    hidden, k_total = 1024, 2048
+    K = k_total // world
+    op = pkg.OprojAllReduce(dist.group.WORLD, max_tokens=512, hidden=hidden)
+    g = torch.Generator(device=dev).manual_seed(1234)  # same draws on every rank
+    w_full = (torch.randn(hidden, k_total, generator=g, device=dev) * 0.03).to(torch.bfloat16)
+    w = w_full[:, rank * K:(rank + 1) * K].contiguous()
+    worst = 0.0
+    for step, M in enumerate([512, 100, 1, 300, 512, 257, 64, 512]):
+        a_full = (torch.randn(M, k_total, generator=g, device=dev)).to(torch.bfloat16)
+        a = a_full[:, rank * K:(rank + 1) * K].contiguous()
+        y = op(a, w)
+        # reference 1: sum over ranks of each rank's bf16 partial, in fp32, rounded once
+        parts = [(a_full[:, r * K:(r + 1) * K].float() @ w_full[:, r * K:(r + 1) * K].float().T).bfloat16()
+                 for r in range(world)]
+        ref = torch.stack([p.float() for p in parts]).sum(0).bfloat16()
+        # reference 2: the reference engine's path, F.linear then NCCL all-reduce
+        y_nccl = torch.nn.functional.linear(a, w)
+        dist.all_reduce(y_nccl)
+        torch.cuda.synchronize()
+        scale = ref.float().abs().max().item()
+        d1 = (y.float() - ref.float()).abs().max().item() / scale
+        d2 = (y.float() - y_nccl.float()).abs().max().item() / scale
+        worst = max(worst, d1, d2)
+        assert torch.isfinite(y.float()).all()
+        assert d1 <= 2 ** -6 and d2 <= 2 ** -6, (step, M, d1, d2)
+        # every rank holds the same bits
+        gathered = [torch.empty_like(y) for _ in range(world)]
+        dist.all_gather(gathered, y)
+        assert all(torch.equal(gathered[0], t) for t in gathered), "ranks disagree"
+    assert op.error() == 0, "a bounded wait gave up"
+    print(json.dumps({"rank": rank, "world": world, "epochs": op.epoch, "worst_rel": worst}), flush=True)
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
