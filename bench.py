@@ -514,7 +514,7 @@ def run_oproj(args, pkg, torch, dev, world, rank):
     g = torch.Generator(device=dev).manual_seed(7 + rank)
     w = (torch.randn(hidden, K, generator=g, device=dev) * 0.02).to(torch.bfloat16)
     stream = torch.cuda.current_stream(dev)
-    for M in (512, 64):
+    for M in (512, 64, 8):
         a = torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16)
 
         def fused():
@@ -524,24 +524,49 @@ def run_oproj(args, pkg, torch, dev, world, rank):
             y = torch.nn.functional.linear(a, w)
             dist.all_reduce(y)
         times = {}
-        for name, fn in (("fused", fused), ("reference", reference)):
-            for _ in range(max(args.warmup, 3)):
-                fn()
+
+        def device_us(run, calls):
             torch.cuda.synchronize()
             dist.barrier(device_ids=[dev.index])
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
-            for _ in range(args.steps):
-                fn()
+            run()
             e1.record(stream)
             torch.cuda.synchronize()
-            t = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev)
+            t = torch.tensor([e0.elapsed_time(e1) / calls], device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            times[name] = t.item() * 1e3
+            return t.item() * 1e3
+
+        for name, fn in (("fused", fused), ("reference", reference)):
+            for _ in range(max(args.warmup, 3)):
+                fn()
+
+            def eager():
+                for _ in range(args.steps):
+                    fn()
+            times[name] = device_us(eager, args.steps)
+            # as nano-vLLM's decode runs it: captured in a CUDA graph (20 calls per replay)
+            graph, side = torch.cuda.CUDAGraph(), torch.cuda.Stream(dev)
+            side.wait_stream(stream)
+            with torch.cuda.stream(side), torch.cuda.graph(graph, stream=side):
+                for _ in range(20):
+                    fn()
+            stream.wait_stream(side)
+            graph.replay()
+            reps = max(1, args.steps // 20)
+
+            def replay():
+                for _ in range(reps):
+                    graph.replay()
+            times[name + "_graph"] = device_us(replay, reps * 20)
+            del graph
         flops = 2.0 * M * hidden * k_total
         results[f"M={M}"] = {"fused_us": round(times["fused"], 2), "reference_us": round(times["reference"], 2),
                              "speedup": round(times["reference"] / times["fused"], 2),
-                             "fused_TFLOPs_total": round(flops / (times["fused"] * 1e-6) / 1e12, 1),
+                             "fused_graph_us": round(times["fused_graph"], 2),
+                             "reference_graph_us": round(times["reference_graph"], 2),
+                             "graph_speedup": round(times["reference_graph"] / times["fused_graph"], 2),
+                             "fused_TFLOPs_total": round(flops / (times["fused_graph"] * 1e-6) / 1e12, 1),
                              "nvlink_bytes_in_per_rank": (world - 1) * M * hidden * 2}
     assert op.error() == 0
     if rank == 0:
@@ -549,7 +574,7 @@ def run_oproj(args, pkg, torch, dev, world, rank):
                           "unit": "us", "higher_is_better": False, "n_gpus": world, "steps": args.steps,
                           "warmup": args.warmup, "dtype": "bf16", "data": "synthetic",
                           "config": {"workload": f"Qwen3-8B o_proj, hidden 4096, tp{world}"},
-                          "value": results["M=512"]["fused_us"], "cases": results}), flush=True)
+                          "value": results["M=512"]["fused_graph_us"], "cases": results}), flush=True)
     dist.destroy_process_group()
 
 

@@ -150,23 +150,33 @@ B200_API int32_t b200_decode_metadata(const int32_t* packed, int32_t batch, int3
  * (nanovllm/layers/linear.py:152-156, called at nanovllm/models/qwen3.py:87):
  *     y = F.linear(a, w)   (a [M, K] this rank's shard, w [N, K]; bf16)
  *     dist.all_reduce(y)
- * One launch per rank: tcgen05 GEMM tiles of y_r (rounded to bf16) go to this
- * rank's slot buffer and are announced with release flags; then every tile is
- * summed over the ranks' slots (plain loads over NVLink, fp32, rank order, so
- * all ranks get the same bits) into out [M, N] (row stride ldo).
+ * One launch per rank: tcgen05 GEMM units (128 x 256 tiles, split along K
+ * when there are fewer tiles than SMs, split partials summed in fp32 in split
+ * order) are rounded to bf16 and stored straight into every rank's slot
+ * buffer (plain stores over NVLink), announced with system-scope release
+ * flags; then every rank sums the ranks' partials from its own slot buffer
+ * (fp32, rank order, so all ranks get the same bits) into out [M, N] (row
+ * stride ldo).
  * slots[r] / flags[r]: device arrays of every rank's buffers, mapped into this
- * process (e.g. CUDA symmetric memory): slots [2][slot_rows][N] bf16, flags
- * uint32 [max_tiles + 2] zeroed once before the first call.  epoch: 1, 2, 3,
- * ... the same sequence on every rank (one call per epoch).  N % 256 == 0,
- * K % 64 == 0, M <= slot_rows; a, w 16-byte aligned with strides that are
- * multiples of 8 elements.  Bounded waits set the error word read by
- * b200_oproj_allreduce_error (results of that call undefined).
+ * process (e.g. CUDA symmetric memory): slots [2][world][slot_rows][N] bf16,
+ * flags uint32 [max_units * world + 2] zeroed once before the first call.  The
+ * call's epoch lives in the flag words, so the launch may be captured in a
+ * CUDA graph; every rank makes the same calls in the same order.  workspace:
+ * b200_oproj_allreduce_workspace_size() bytes of this rank's memory, zeroed
+ * once (NULL disables the K split).  max_units >= the tile count
+ * ceil(M/128) * N/256; the K split never makes more units than max_units.
+ * N % 256 == 0, K % 64 == 0, M <= slot_rows; a, w 16-byte aligned with
+ * strides that are multiples of 8 elements.  Bounded waits set the error word
+ * read by b200_oproj_allreduce_error (results of that call undefined).
  */
 B200_API int32_t b200_oproj_allreduce(void* out, int64_t ldo, const void* a, int64_t lda,
                              const void* w, int64_t ldw, int32_t M, int32_t N, int32_t K,
                              void* const* slots, int32_t slot_rows,
-                             uint32_t* const* flags, int32_t max_tiles,
-                             int32_t rank, int32_t world, uint32_t epoch, void* stream);
+                             uint32_t* const* flags, int32_t max_units,
+                             void* workspace, int64_t workspace_bytes,
+                             int32_t rank, int32_t world, void* stream);
+
+B200_API int64_t b200_oproj_allreduce_workspace_size(void);
 
 B200_API int32_t b200_oproj_allreduce_error(void* stream, int32_t* flag);
 

@@ -4,23 +4,40 @@
 // nanovllm/layers/linear.py:152-156):
 //     y = F.linear(x_r, W_r)          (this rank's K shard, rounded to bf16)
 //     dist.all_reduce(y)              (sum over ranks)
-// in one kernel per rank, over buffers every rank can read (CUDA symmetric
-// memory; peers are reached with plain loads over NVLink, no multicast):
-//   phase 1: persistent CTAs compute 128 x 256 output tiles of y_r with
-//            tcgen05 (TMA loads without multicast, SS MMA M=128 N=256, fp32
-//            accumulators in tensor memory), round them to bf16, store them
-//            in this rank's slot buffer and publish each tile with a
-//            system-scope release of its ready flag (= the call's epoch);
-//   phase 2: for the same tiles, each CTA waits (bounded) for every rank's
-//            ready flag, sums the ranks' bf16 tiles in fp32 in rank order
-//            (so every rank gets the same bits) and writes bf16 y.
-// Phase 1 never waits on a peer, so phase 2's waits always end.  Slot buffers
-// ([2][slot_rows][N] per rank) alternate by epoch parity; the grid's last CTA
-// to finish phase 2 publishes the rank's done epoch, and a call waits for
-// every rank's done epoch >= epoch - 2 before rewriting its slot (the one
-// read two calls ago).  Waits give up after kWaitLimitNs and set the error
-// word.  Flags per rank (uint32, zeroed once): [max_tiles] ready epochs,
-// then the done epoch, then a local finished-CTA counter.
+// in one kernel per rank over buffers every rank can address (CUDA symmetric
+// memory; peers are reached with plain stores over NVLink, no multicast).
+//
+// Work unit = (128 x 256 output tile, K split).  Few tiles (decode batches)
+// are split along K so that every SM has a unit; many tiles run unsplit on
+// persistent CTAs.
+//   phase 1  tcgen05 GEMM: TMA loads (no multicast), SS MMA M=128 N=256 into
+//            one of two fp32 accumulators in tensor memory.  Unsplit tiles are
+//            rounded to bf16 and PUSHED into every rank's slot buffer (this
+//            rank's source region), then published with a system-scope release
+//            of a ready flag on every rank (after a CTA barrier: the release is
+//            cumulative, so no per-thread system fence is needed).  Split tiles
+//            stage their fp32 partial in shared memory and write it to a local
+//            workspace with one bulk copy, then release a local arrival flag.
+//   phase 1b (split tiles) each of a tile's `splits` CTAs sums the tile's fp32
+//            partials for its share of the rows, in split order (deterministic),
+//            rounds to bf16 and pushes / publishes as above.
+//   phase 2  for its rows, each CTA waits (bounded) for every rank's ready flag,
+//            sums the ranks' bf16 partials from LOCAL memory in fp32 in rank
+//            order (every rank gets the same bits) and writes bf16 y.
+// Phases 1 and 1b wait only on CTAs of this grid on this GPU (all resident: the
+// grid never exceeds the SM count and a CTA fills an SM), so phase 2's waits end.
+//
+// Epochs: the call's epoch is read from this rank's flag words (the grid's last
+// CTA of the previous call left it there), so a launch captured in a CUDA graph
+// stays correct.  Slot buffers [2][world][slot_rows][N] alternate by epoch
+// parity.  Rewriting a slot needs no extra handshake: a rank pushes epoch e+2
+// only after its own call e+1 ended, which waited for every rank's e+1 ready
+// flags; a rank publishes those only after its call e (its last read of that
+// parity) ended.  Unit 0 always has rows, so every call carries such a flag.
+// All epoch comparisons are wrap-safe.  Waits poll with one lane per flag, give
+// up after kWaitLimitNs and set the error word.  Flag words per rank (uint32,
+// zeroed once): [max_units][world] ready epochs, a finished-CTA counter, the
+// last epoch.
 #include "common.cuh"
 #include "tcgen05.cuh"
 
@@ -28,27 +45,30 @@ namespace b200 {
 namespace oar {
 
 constexpr int kBM = 128, kBN = 256, kBK = 64, kStages = 4;
-constexpr int kThreads = 192;  // warp 0 TMA, warp 1 MMA + TMEM owner, warps 2-5 epilogue; all reduce
+constexpr int kThreads = 192;  // warp 0 TMA, warp 1 MMA + TMEM owner, warps 2-5 epilogue; all: 1b, 2
 constexpr int kABytes = kBM * kBK * 2, kBBytes = kBN * kBK * 2;
-constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kTmemCols = 512;  // two 256-column fp32 accumulators
+constexpr int kMaxSplits = 16;
+constexpr int kArriveWords = 256;  // workspace head: per-unit split arrival epochs (units <= SM count)
 
 struct Params {
     uint16_t* out;
     int64_t ldo;
-    int32_t M, N, K, rank, world, tiles_n, num_tiles;
-    uint32_t epoch;
-    uint16_t* const* slots;  // [world] -> each rank's slot buffers: [2][slot_rows][N] bf16
-    uint32_t* const* flags;  // [world] -> each rank's flags: [max_tiles] ready, done epoch, CTA counter
-    int32_t max_tiles, slot_rows;
+    int32_t M, N, K, rank, world, tiles_n, splits, num_units, kb_count;
+    uint16_t* const* slots;  // [world] -> each rank's slots: [2][world][slot_rows][N] bf16
+    uint32_t* const* flags;  // [world] -> each rank's flag words
+    int32_t max_units, slot_rows;
+    uint32_t* arrive;  // local [kArriveWords] split arrival epochs
+    float* part;       // local [units][kBM][kBN] fp32 split partials
 };
 
 struct Smem {
-    uint8_t a[kStages][kABytes];
+    uint8_t a[kStages][kABytes];  // a and b are contiguous: phase 1b stages partials here
     uint8_t b[kStages][kBBytes];
     uint64_t full[kStages], empty[kStages];
-    uint64_t acc_full, acc_empty, drain;
+    uint64_t acc_full[2], acc_empty[2], drain, fix;
     uint32_t tmem_base;
-    int32_t err;
+    int32_t err, ok;
 };
 
 __device__ int32_t g_oar_error;
@@ -58,24 +78,94 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Bulk copy shared -> global (no multicast): start, then wait until the writes are performed.
+// Every thread that wrote the source executed fence_proxy_async_smem() before the barrier
+// that precedes this call.
+__device__ __forceinline__ void bulk_store_wait(void* dst, const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(reinterpret_cast<uint64_t>(dst)),
+                 "r"(smem_u32(src)), "r"(bytes)
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
 
-// Bounded wait until *flag >= epoch (epochs only grow); false on timeout.
-__device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t epoch) {
-    if (ld_acquire_sys(flag) >= epoch) return true;
+// v has reached `target` on a wrapping uint32 epoch counter
+__device__ __forceinline__ bool reached(uint32_t v, uint32_t target) { return int32_t(v - target) >= 0; }
+
+// Whole warp: lane l < n waits until flags[l * stride] reaches epoch, all lanes in
+// parallel; true in every lane once all have, false in every lane on timeout.
+template <bool SYS>
+__device__ __forceinline__ bool warp_wait_flags(const uint32_t* flags, int stride, int n, uint32_t epoch) {
+    const int lane = threadIdx.x & 31;
+    auto ok = [&]() {
+        if (lane >= n) return true;
+        const uint32_t* f = flags + lane * stride;
+        return reached(SYS ? ld_acquire_sys(f) : ld_acquire_gpu(f), epoch);
+    };
+    bool done = ok();
+    if (__all_sync(0xffffffffu, done)) return true;
     const uint64_t t0 = global_timer_ns();
     while (true) {
-        if (ld_acquire_sys(flag) >= epoch) return true;
-        if (global_timer_ns() - t0 > kWaitLimitNs) return false;
-        __nanosleep(64);
+        if (!done) done = ok();
+        if (__all_sync(0xffffffffu, done)) return true;
+        if (__shfl_sync(0xffffffffu, global_timer_ns() - t0 > kWaitLimitNs, 0)) return false;
+        __nanosleep(32);
     }
+}
+
+// Named barrier that returns, to every participating thread, the OR of `pred`:
+// loop exits decided with it are uniform, so no thread is left at a later barrier.
+__device__ __forceinline__ bool named_bar_any(int id, int threads, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n.reg .pred p, q;\nsetp.ne.u32 p, %1, 0;\nbar.red.or.pred q, %2, %3, p;\nselp.u32 %0, 1, 0, q;\n}"
+        : "=r"(r)
+        : "r"(uint32_t(pred)), "r"(id), "r"(threads)
+        : "memory");
+    return r != 0;
 }
 
 __device__ __forceinline__ void flag_error(Smem& sm, int code) {
     atomicOr(&g_oar_error, code);
     *reinterpret_cast<volatile int32_t*>(&sm.err) = 1;
+}
+
+// Rows [r0, r1) of unit u's tile that unit u reduces (phase 1b) and all-reduces (phase 2).
+struct UnitRows {
+    int t, s, m0, n0, r0, r1;
+};
+__device__ __forceinline__ UnitRows unit_rows(const Params& p, int u) {
+    UnitRows r;
+    r.t = u / p.splits;
+    r.s = u - r.t * p.splits;
+    r.m0 = (r.t / p.tiles_n) * kBM;
+    r.n0 = (r.t % p.tiles_n) * kBN;
+    const int valid = min(kBM, p.M - r.m0);
+    const int per = (valid + p.splits - 1) / p.splits;
+    r.r0 = min(valid, r.s * per);
+    r.r1 = min(valid, r.r0 + per);
+    return r;
+}
+
+__device__ __forceinline__ uint4 pack8(const float* v) {
+    uint4 o;
+    o.x = pack2<true>(v[0], v[1]);
+    o.y = pack2<true>(v[2], v[3]);
+    o.z = pack2<true>(v[4], v[5]);
+    o.w = pack2<true>(v[6], v[7]);
+    return o;
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -84,28 +174,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     extern __shared__ uint8_t smem_raw[];
     Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int kb_count = (p.K + kBK - 1) / kBK;
-    const int parity = p.epoch & 1;
     uint32_t* my_flags = p.flags[p.rank];
-    uint16_t* my_slot = p.slots[p.rank] + size_t(parity) * p.slot_rows * p.N;
+    const int fl_count = p.max_units * p.world;  // finished-CTA counter, then the last epoch
+    const uint32_t epoch = __ldcg(my_flags + fl_count + 1) + 1u;
+    const int parity = epoch & 1;
+    const size_t slot_half = size_t(p.world) * p.slot_rows * p.N;
+    // this rank's source region inside every rank's slot buffer
+    const size_t push_off = size_t(parity) * slot_half + size_t(p.rank) * p.slot_rows * p.N;
 
     if (tid == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&sm.full[s], 1);
             mbar_init(&sm.empty[s], 1);
         }
-        mbar_init(&sm.acc_full, 1);
-        mbar_init(&sm.acc_empty, 128);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&sm.acc_full[b], 1);
+            mbar_init(&sm.acc_empty[b], 128);
+        }
         mbar_init(&sm.drain, 1);
+        mbar_init(&sm.fix, 1);
         sm.err = 0;
         fence_mbar_init();
-        // this call rewrites the slot every rank read two calls ago
-        if (p.epoch > 2)
-            for (int r = 0; r < p.world; ++r)
-                if (!wait_flag(p.flags[r] + p.max_tiles, p.epoch - 2)) {
-                    atomicOr(&g_oar_error, 8);
-                    sm.err = 1;
-                }
     }
     if (warp == 1) {
         tc::tmem_alloc(&sm.tmem_base, kTmemCols);
@@ -122,19 +211,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             prefetch_tmap(&tma);
             prefetch_tmap(&tmb);
-            const uint64_t pol = l2_policy_evict_first();
+            const uint64_t pol_a = l2_policy_evict_last(), pol_w = l2_policy_evict_first();
             int g = 0;
-            for (int t = blockIdx.x; t < p.num_tiles && !failed(); t += gridDim.x) {
-                const int m0 = (t / p.tiles_n) * kBM, n0 = (t % p.tiles_n) * kBN;
-                for (int kb = 0; kb < kb_count; ++kb, ++g) {
+            for (int u = blockIdx.x; u < p.num_units && !failed(); u += gridDim.x) {
+                const UnitRows ur = unit_rows(p, u);
+                const int kb0 = ur.s * p.kb_count / p.splits, kb1 = (ur.s + 1) * p.kb_count / p.splits;
+                for (int kb = kb0; kb < kb1; ++kb, ++g) {
                     const int st = g % kStages;
                     if (!mbar_wait(&sm.empty[st], ((g / kStages) & 1) ^ 1)) { flag_error(sm, 1); break; }
                     mbar_arrive_expect_tx(&sm.full[st], kABytes + kBBytes);
-                    tma_load_2d(sm.a[st], &tma, kb * kBK, m0, &sm.full[st], pol);
-                    tma_load_2d(sm.b[st], &tmb, kb * kBK, n0, &sm.full[st], pol);
+                    tma_load_2d(sm.a[st], &tma, kb * kBK, ur.m0, &sm.full[st], pol_a);
+                    tma_load_2d(sm.b[st], &tmb, kb * kBK, ur.n0, &sm.full[st], pol_w);
                 }
             }
-            // every load issued above has landed before the CTA exits (bounded)
+            // every load issued above has landed before the stages are reused or the CTA exits (bounded)
             for (int st = 0; st < kStages && st < g; ++st) {
                 const int last = st + ((g - 1 - st) / kStages) * kStages;
                 mbar_wait(&sm.full[st], (last / kStages) & 1);
@@ -144,22 +234,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             constexpr uint32_t idesc = tc::idesc_f16<true>(kBM, kBN, false, false);
             int g = 0, n_acc = 0;
-            for (int t = blockIdx.x; t < p.num_tiles && !failed(); t += gridDim.x, ++n_acc) {
-                // the epilogue must have read the previous tile's accumulator
-                if (n_acc > 0 && !mbar_wait(&sm.acc_empty, (n_acc - 1) & 1)) { flag_error(sm, 2); break; }
+            for (int u = blockIdx.x; u < p.num_units && !failed(); u += gridDim.x, ++n_acc) {
+                const UnitRows ur = unit_rows(p, u);
+                const int kb0 = ur.s * p.kb_count / p.splits, kb1 = (ur.s + 1) * p.kb_count / p.splits;
+                const int buf = n_acc & 1;
+                // the epilogue has read this accumulator's previous unit
+                if (n_acc >= 2 && !mbar_wait(&sm.acc_empty[buf], ((n_acc >> 1) - 1) & 1)) {
+                    flag_error(sm, 2);
+                    break;
+                }
                 tc::fence_after_sync();
-                for (int kb = 0; kb < kb_count; ++kb, ++g) {
+                const uint32_t acc = tmem + uint32_t(buf * kBN);
+                for (int kb = kb0; kb < kb1; ++kb, ++g) {
                     const int st = g % kStages;
                     if (!mbar_wait(&sm.full[st], (g / kStages) & 1)) { flag_error(sm, 2); break; }
                     tc::fence_after_sync();
                     const uint32_t aa = smem_u32(sm.a[st]), ba = smem_u32(sm.b[st]);
 #pragma unroll
                     for (int kk = 0; kk < kBK / 16; ++kk)
-                        tc::mma_ss(tmem, tc::smem_desc_sw128(aa + kk * 32, 16, 1024),
-                                   tc::smem_desc_sw128(ba + kk * 32, 16, 1024), idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                        tc::mma_ss(acc, tc::smem_desc_sw128(aa + kk * 32, 16, 1024),
+                                   tc::smem_desc_sw128(ba + kk * 32, 16, 1024), idesc,
+                                   (kb > kb0 || kk > 0) ? 1u : 0u);
                     tc::commit(&sm.empty[st]);
                 }
-                tc::commit(&sm.acc_full);
+                tc::commit(&sm.acc_full[buf]);
             }
             tc::commit(&sm.drain);  // every MMA issued above has completed before TMEM is freed
             mbar_wait(&sm.drain, 0);
@@ -168,36 +266,65 @@ __global__ void __launch_bounds__(kThreads, 1)
         // epilogue: warp w reads TMEM lanes 32*(w%4).., one output row per thread
         const int q = warp & 3, row_in = q * 32 + lane;
         int n_acc = 0;
-        for (int t = blockIdx.x; t < p.num_tiles && !failed(); t += gridDim.x, ++n_acc) {
-            const int m0 = (t / p.tiles_n) * kBM, n0 = (t % p.tiles_n) * kBN;
-            if (!mbar_wait(&sm.acc_full, n_acc & 1)) { flag_error(sm, 4); break; }
+        for (int u = blockIdx.x; u < p.num_units; u += gridDim.x, ++n_acc) {
+            const UnitRows ur = unit_rows(p, u);
+            const int buf = n_acc & 1;
+            const bool got = mbar_wait(&sm.acc_full[buf], (n_acc >> 1) & 1);
+            if (!got) flag_error(sm, 4);
+            if (named_bar_any(1, 128, !got || failed())) break;
             tc::fence_after_sync();
-            const int row = m0 + row_in;
-            const uint32_t lane_addr = uint32_t(q * 32) << 16;
+            const uint32_t taddr = tmem + uint32_t(buf * kBN) + (uint32_t(q * 32) << 16);
+            const bool live = row_in < ur.r1;  // unsplit: r0 = 0, r1 = valid rows
+            if (p.splits == 1) {
+                const size_t row_off = push_off + size_t(ur.m0 + row_in) * p.N + ur.n0;
 #pragma unroll 1
-            for (int c = 0; c < kBN / 32; ++c) {
-                float v[32];
-                tc::tmem_ld32(tmem + lane_addr + c * 32, v);
-                tc::tmem_wait_ld();
-                if (row < p.M) {
-                    uint4* dst = reinterpret_cast<uint4*>(my_slot + size_t(row) * p.N + n0 + c * 32);
-#pragma unroll
-                    for (int e = 0; e < 32; e += 8) {
-                        uint4 o;
-                        o.x = pack2<true>(v[e], v[e + 1]);
-                        o.y = pack2<true>(v[e + 2], v[e + 3]);
-                        o.z = pack2<true>(v[e + 4], v[e + 5]);
-                        o.w = pack2<true>(v[e + 6], v[e + 7]);
-                        dst[e / 8] = o;
+                for (int c = 0; c < kBN / 32; ++c) {
+                    float v[32];
+                    tc::tmem_ld32(taddr + c * 32, v);
+                    tc::tmem_wait_ld();
+                    if (live) {
+                        const uint4 o0 = pack8(v), o1 = pack8(v + 8), o2 = pack8(v + 16), o3 = pack8(v + 24);
+                        for (int r = 0; r < p.world; ++r) {
+                            uint4* dst = reinterpret_cast<uint4*>(p.slots[r] + row_off + c * 32);
+                            dst[0] = o0;
+                            dst[1] = o1;
+                            dst[2] = o2;
+                            dst[3] = o3;
+                        }
                     }
                 }
+                tc::fence_before_sync();
+                mbar_arrive(&sm.acc_empty[buf]);
+                // publish: every epilogue thread's stores, then one system-scope release per rank
+                named_bar_sync(1, 128);
+                if (row_in < p.world) st_release_sys(p.flags[row_in] + u * p.world + p.rank, epoch);
+            } else {
+                // One unit per CTA: every MMA has completed, so the operand stages are free.
+                // Row r's 16-byte chunk j goes to chunk j ^ (r & 7) of its 1 KB row (conflict-free
+                // stores); the summing side undoes the swizzle.
+                float* srow = reinterpret_cast<float*>(&sm.a[0][0]) + row_in * kBN;
+                const int valid = min(kBM, p.M - ur.m0);
+#pragma unroll 1
+                for (int c = 0; c < kBN / 32; ++c) {
+                    float v[32];
+                    tc::tmem_ld32(taddr + c * 32, v);
+                    tc::tmem_wait_ld();
+                    if (row_in < valid) {
+#pragma unroll
+                        for (int e = 0; e < 8; ++e)
+                            *reinterpret_cast<float4*>(srow + (((c * 8 + e) ^ (row_in & 7)) * 4)) =
+                                make_float4(v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3]);
+                    }
+                }
+                fence_proxy_async_smem();
+                tc::fence_before_sync();
+                mbar_arrive(&sm.acc_empty[buf]);
+                named_bar_sync(1, 128);
+                if (row_in == 0) {
+                    bulk_store_wait(p.part + size_t(u) * kBM * kBN, &sm.a[0][0], uint32_t(valid) * kBN * 4);
+                    st_release_gpu(p.arrive + u, epoch);
+                }
             }
-            tc::fence_before_sync();
-            mbar_arrive(&sm.acc_empty);
-            // publish the tile: every epilogue thread's stores, then one system-scope release
-            __threadfence_system();
-            named_bar_sync(1, 128);
-            if (row_in == 0) st_release_sys(my_flags + t, p.epoch);
         }
     }
     tc::fence_before_sync();
@@ -207,54 +334,120 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::tmem_dealloc(tmem, kTmemCols);
     }
 
-    // ------------------------------------------------------------------ phase 2
-    __shared__ int ready_ok;
-    const uint16_t* const* slots = p.slots;
-    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
-        const int m0 = (t / p.tiles_n) * kBM, n0 = (t % p.tiles_n) * kBN;
-        if (tid == 0) {
-            int ok = !failed();
-            for (int r = 0; r < p.world && ok; ++r)
-                if (!wait_flag(p.flags[r] + t, p.epoch)) ok = 0;
-            if (!ok) flag_error(sm, 16);
-            ready_ok = ok;
+    // ----------------------------------------------------------------- phase 1b
+    if (p.splits > 1) {
+        const int u = blockIdx.x;  // one unit per CTA when split
+        const UnitRows ur = unit_rows(p, u);
+        float* stage = reinterpret_cast<float*>(&sm.a[0][0]);
+        const uint32_t part_bytes = uint32_t(ur.r1 - ur.r0) * kBN * 4;
+        if (warp == 0) {
+            // every lane takes part in the warp-collective wait
+            const bool arrived = warp_wait_flags<false>(p.arrive + ur.t * p.splits, 1, p.splits, epoch);
+            const bool ok = arrived && !failed();
+            if (!ok && lane == 0) flag_error(sm, 32);
+            if (ok && part_bytes && lane == 0) {
+                // the partials were written through the generic proxy; the bulk copies read them
+                asm volatile("fence.proxy.async.global;" ::: "memory");
+                mbar_arrive_expect_tx(&sm.fix, part_bytes * p.splits);
+                for (int s = 0; s < p.splits; ++s)
+                    bulk_load(reinterpret_cast<uint8_t*>(stage) + size_t(s) * part_bytes,
+                              p.part + (size_t(ur.t * p.splits + s) * kBM + ur.r0) * kBN, part_bytes, &sm.fix);
+            }
+            if (lane == 0) sm.ok = ok;
         }
         __syncthreads();
-        if (!ready_ok) break;
-        // 128 x 256 bf16 tile = 4096 16-byte groups; sum the ranks' copies in rank order
-        for (int i = tid; i < kBM * kBN / 8; i += kThreads) {
-            const int r_in = i / (kBN / 8), c8 = i % (kBN / 8);
-            const int row = m0 + r_in;
-            if (row >= p.M) continue;
-            const size_t off = size_t(parity) * p.slot_rows * p.N + size_t(row) * p.N + n0 + c8 * 8;
-            float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-            for (int r = 0; r < p.world; ++r) {
-                const uint4 v = __ldcg(reinterpret_cast<const uint4*>(slots[r] + off));
-                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        const bool go = sm.ok && part_bytes && !failed();
+        if (go) {
+            if (!mbar_wait(&sm.fix, 0)) flag_error(sm, 32);
+            const int items = (ur.r1 - ur.r0) * (kBN / 8);
+            const int part_floats = (ur.r1 - ur.r0) * kBN;
+            for (int i = tid; i < items && !failed(); i += kThreads) {
+                // item i: physical chunks 2k, 2k+1 of its staged row hold logical chunks
+                // (2k, 2k+1) ^ (row & 7): the 8 columns at 8 * (k ^ ((row & 7) >> 1)), swapped
+                // halves when row is odd
+                float acc[8];
+                const float4* s0 = reinterpret_cast<const float4*>(stage + i * 8);
+                float4 x = s0[0], y = s0[1];
+                acc[0] = x.x, acc[1] = x.y, acc[2] = x.z, acc[3] = x.w;
+                acc[4] = y.x, acc[5] = y.y, acc[6] = y.z, acc[7] = y.w;
+                for (int s = 1; s < p.splits; ++s) {
+                    const float4* sp = reinterpret_cast<const float4*>(stage + size_t(s) * part_floats + i * 8);
+                    x = sp[0];
+                    y = sp[1];
+                    acc[0] += x.x, acc[1] += x.y, acc[2] += x.z, acc[3] += x.w;
+                    acc[4] += y.x, acc[5] += y.y, acc[6] += y.z, acc[7] += y.w;
+                }
+                const int row = ur.r0 + i / (kBN / 8), k = i % (kBN / 8);
+                const int sw = row & 7, c8 = k ^ (sw >> 1);
+                uint4 o = pack8(acc);
+                if (sw & 1) o = make_uint4(o.z, o.w, o.x, o.y);
+                const size_t off = push_off + size_t(ur.m0 + row) * p.N + ur.n0 + c8 * 8;
+                for (int r = 0; r < p.world; ++r) *reinterpret_cast<uint4*>(p.slots[r] + off) = o;
+            }
+        }
+        __syncthreads();
+        if (go && !failed() && tid < p.world) st_release_sys(p.flags[tid] + u * p.world + p.rank, epoch);
+    }
+
+    // ------------------------------------------------------------------ phase 2
+    const uint16_t* local = p.slots[p.rank] + size_t(parity) * slot_half;
+    const size_t src_stride = size_t(p.slot_rows) * p.N;
+    for (int u = blockIdx.x; u < p.num_units; u += gridDim.x) {
+        const UnitRows ur = unit_rows(p, u);
+        if (ur.r0 >= ur.r1) continue;
+        if (warp == 0) {
+            const bool ready = warp_wait_flags<true>(my_flags + u * p.world, 1, p.world, epoch);
+            const bool ok = ready && !failed();
+            if (lane == 0) {
+                if (!ok) flag_error(sm, 16);
+                sm.ok = ok;
+            }
+        }
+        __syncthreads();
+        if (!sm.ok) break;
+        const int items = (ur.r1 - ur.r0) * (kBN / 8);
+        constexpr int kU = 4;
+        for (int i0 = tid; i0 < items; i0 += kThreads * kU) {
+            float acc[kU][8];
+            size_t off[kU];
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    acc[2 * e] += __uint_as_float(w[e] << 16);
-                    acc[2 * e + 1] += __uint_as_float(w[e] & 0xFFFF0000u);
+            for (int j = 0; j < kU; ++j) {
+                const int i = min(i0 + j * kThreads, items - 1);
+                off[j] = size_t(ur.m0 + ur.r0 + i / (kBN / 8)) * p.N + ur.n0 + (i % (kBN / 8)) * 8;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) acc[j][e] = 0.f;
+            }
+            for (int r = 0; r < p.world; ++r) {
+                uint4 v[kU];
+#pragma unroll
+                for (int j = 0; j < kU; ++j) v[j] = __ldcg(reinterpret_cast<const uint4*>(local + r * src_stride + off[j]));
+#pragma unroll
+                for (int j = 0; j < kU; ++j) {
+                    const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        acc[j][2 * e] += __uint_as_float(w[e] << 16);
+                        acc[j][2 * e + 1] += __uint_as_float(w[e] & 0xFFFF0000u);
+                    }
                 }
             }
-            uint4 o;
-            o.x = pack2<true>(acc[0], acc[1]);
-            o.y = pack2<true>(acc[2], acc[3]);
-            o.z = pack2<true>(acc[4], acc[5]);
-            o.w = pack2<true>(acc[6], acc[7]);
-            *reinterpret_cast<uint4*>(p.out + int64_t(row) * p.ldo + n0 + c8 * 8) = o;
+#pragma unroll
+            for (int j = 0; j < kU; ++j) {
+                const int i = i0 + j * kThreads;
+                if (i >= items) break;
+                const int row = ur.m0 + ur.r0 + i / (kBN / 8);
+                *reinterpret_cast<uint4*>(p.out + int64_t(row) * p.ldo + ur.n0 + (i % (kBN / 8)) * 8) = pack8(acc[j]);
+            }
         }
         __syncthreads();
     }
-    // The last CTA to finish publishes that this rank has read every slot of this epoch.
+    // The last CTA to finish (every CTA has read the epoch by then) leaves it for the next call.
     __syncthreads();
     if (tid == 0) {
-        __threadfence();
-        const uint32_t prev = atomicAdd(my_flags + p.max_tiles + 1, 1u);
+        const uint32_t prev = atomicAdd(my_flags + fl_count, 1u);
         if (prev == gridDim.x - 1) {
-            __threadfence();
-            my_flags[p.max_tiles + 1] = 0;
-            st_release_sys(my_flags + p.max_tiles, p.epoch);
+            my_flags[fl_count] = 0;
+            my_flags[fl_count + 1] = epoch;
         }
     }
 }
@@ -262,10 +455,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 }  // namespace oar
 }  // namespace b200
 
+extern "C" int64_t b200_oproj_allreduce_workspace_size(void) {
+    using namespace b200;
+    return int64_t(oar::kArriveWords) * 4 + int64_t(device_sm_count()) * oar::kBM * oar::kBN * 4;
+}
+
 extern "C" int32_t b200_oproj_allreduce(void* out, int64_t ldo, const void* a, int64_t lda, const void* w,
                                         int64_t ldw, int32_t M, int32_t N, int32_t K, void* const* slots,
-                                        int32_t slot_rows, uint32_t* const* flags, int32_t max_tiles,
-                                        int32_t rank, int32_t world, uint32_t epoch, void* stream) {
+                                        int32_t slot_rows, uint32_t* const* flags, int32_t max_units,
+                                        void* workspace, int64_t workspace_bytes, int32_t rank, int32_t world,
+                                        void* stream) {
     using namespace b200;
     using namespace b200::oar;
     clear_error();
@@ -273,14 +472,24 @@ extern "C" int32_t b200_oproj_allreduce(void* out, int64_t ldo, const void* a, i
     if (M == 0) return B200_OK;
     B200_REQUIRE(out && a && w && slots && flags, "oproj_allreduce: null pointer");
     B200_REQUIRE(world >= 1 && rank >= 0 && rank < world, "oproj_allreduce: rank %d of %d", rank, world);
-    B200_REQUIRE(epoch >= 1, "oproj_allreduce: epochs start at 1");
     if (N % kBN != 0 || K % kBK != 0)
         return fail(B200_ERR_UNSUPPORTED, "oproj_allreduce: N %% 256 and K %% 64 must be 0 (N %d, K %d)", N, K);
     B200_REQUIRE(ldo >= N && lda >= K && ldw >= K && ldo % 8 == 0, "oproj_allreduce: strides");
     const int tiles_n = N / kBN, tiles_m = (M + kBM - 1) / kBM;
-    const int num_tiles = tiles_m * tiles_n;
-    B200_REQUIRE(num_tiles <= max_tiles, "oproj_allreduce: %d tiles > flag capacity %d", num_tiles, max_tiles);
+    const int num_tiles = tiles_m * tiles_n, kb_count = K / kBK;
+    const int sms = device_sm_count();
+    B200_REQUIRE(num_tiles <= max_units, "oproj_allreduce: %d tiles > flag capacity %d", num_tiles, max_units);
     B200_REQUIRE(M <= slot_rows, "oproj_allreduce: M %d > slot rows %d", M, slot_rows);
+    // split K while that gives every SM a unit and the workspace holds the partials
+    int splits = 1;
+    if (workspace && workspace_bytes >= b200_oproj_allreduce_workspace_size()) {
+        splits = sms / num_tiles;
+        splits = splits < kMaxSplits ? splits : kMaxSplits;
+        splits = splits < kb_count ? splits : kb_count;
+        if (num_tiles * splits > max_units) splits = max_units / num_tiles;
+        if (num_tiles * splits > kArriveWords) splits = kArriveWords / num_tiles;
+        if (splits < 1) splits = 1;
+    }
     CUtensorMap tma, tmb;
     int32_t rc = make_tmap_2d(&tma, a, uint64_t(K), uint64_t(M), uint64_t(lda) * 2, kBK, kBM, true,
                               CU_TENSOR_MAP_SWIZZLE_128B);
@@ -296,15 +505,18 @@ extern "C" int32_t b200_oproj_allreduce(void* out, int64_t ldo, const void* a, i
     p.rank = rank;
     p.world = world;
     p.tiles_n = tiles_n;
-    p.num_tiles = num_tiles;
-    p.epoch = epoch;
+    p.splits = splits;
+    p.num_units = num_tiles * splits;
+    p.kb_count = kb_count;
     p.slots = reinterpret_cast<uint16_t* const*>(slots);
     p.flags = flags;
-    p.max_tiles = max_tiles;
+    p.max_units = max_units;
     p.slot_rows = slot_rows;
+    p.arrive = static_cast<uint32_t*>(workspace);
+    p.part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kArriveWords * 4);
     const int smem = int(sizeof(Smem)) + 1024;
     ensure_smem_attr((const void*)oproj_allreduce_kernel, smem);
-    const int grid = num_tiles < device_sm_count() ? num_tiles : device_sm_count();
+    const int grid = p.num_units < sms ? p.num_units : sms;
     oproj_allreduce_kernel<<<grid, kThreads, smem, static_cast<cudaStream_t>(stream)>>>(p, tma, tmb);
     B200_CUDA_TRY(cudaGetLastError());
     return B200_OK;

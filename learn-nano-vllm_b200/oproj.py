@@ -2,11 +2,13 @@
 
 OprojAllReduce(group, max_tokens, hidden) allocates, once, every rank's slot and
 flag buffers in CUDA symmetric memory (torch.distributed._symmetric_memory; peers
-are reached with plain loads, no multicast) and exchanges their addresses.  Calling
-it with this rank's attention output a [M, K] and o_proj weight shard w [N, K]
-returns y = sum over ranks of a_r @ w_r^T, as RowParallelLinear.forward followed by
-its all-reduce (nanovllm/layers/linear.py:152-156).  Every rank must make the same
-calls in the same order (each call is one epoch of the buffers' protocol).
+are reached with plain stores, no multicast), exchanges their addresses and
+allocates this rank's split-K workspace.  Calling it with this rank's attention
+output a [M, K] and o_proj weight shard w [N, K] returns y = sum over ranks of
+a_r @ w_r^T, as RowParallelLinear.forward followed by its all-reduce
+(nanovllm/layers/linear.py:152-156).  Every rank must make the same calls in the
+same order; the call counter lives on the device, so calls may be captured in a
+CUDA graph.
 """
 import ctypes
 
@@ -28,9 +30,11 @@ class OprojAllReduce:
         self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
         assert hidden % _BN == 0, "hidden size must be a multiple of 256"
         self.N, self.max_tokens = hidden, max_tokens
-        self.max_tiles = ((max_tokens + 127) // 128) * (hidden // _BN)
-        self.slots = symm_mem.empty(2 * max_tokens * hidden, dtype=torch.bfloat16, device=self.device)
-        self.flags = symm_mem.empty(self.max_tiles + 2, dtype=torch.int32, device=self.device)
+        sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+        # ready flags per work unit: a 128 x 256 tile, or a K split of one (never more units than SMs)
+        self.max_units = max(((max_tokens + 127) // 128) * (hidden // _BN), sms)
+        self.slots = symm_mem.empty(2 * self.world * max_tokens * hidden, dtype=torch.bfloat16, device=self.device)
+        self.flags = symm_mem.empty(self.max_units * self.world + 2, dtype=torch.int32, device=self.device)
         self.flags.zero_()
         h_slots = symm_mem.rendezvous(self.slots, group)
         h_flags = symm_mem.rendezvous(self.flags, group)
@@ -40,7 +44,9 @@ class OprojAllReduce:
         self.slot_ptrs = torch.tensor([b + ds for b in h_slots.buffer_ptrs], dtype=torch.int64, device=self.device)
         self.flag_ptrs = torch.tensor([b + df for b in h_flags.buffer_ptrs], dtype=torch.int64, device=self.device)
         self._handles = (h_slots, h_flags)
-        self.epoch = 0
+        self.workspace = torch.zeros(lib().b200_oproj_allreduce_workspace_size(), dtype=torch.uint8,
+                                     device=self.device)
+        self.calls = 0
         torch.cuda.synchronize(self.device)
         dist.barrier(group)  # every rank's flags are zero before anyone's first call
 
@@ -52,11 +58,12 @@ class OprojAllReduce:
         assert w.shape[1] == K and N == self.N and M <= self.max_tokens
         if out is None:
             out = torch.empty(M, N, dtype=torch.bfloat16, device=a.device)
-        self.epoch += 1
+        self.calls += 1
         rc = lib().b200_oproj_allreduce(out.data_ptr(), out.stride(0), a.data_ptr(), a.stride(0), w.data_ptr(),
                                         w.stride(0), M, N, K, self.slot_ptrs.data_ptr(), self.max_tokens,
-                                        self.flag_ptrs.data_ptr(), self.max_tiles, self.rank, self.world,
-                                        self.epoch, torch.cuda.current_stream(a.device).cuda_stream)
+                                        self.flag_ptrs.data_ptr(), self.max_units, self.workspace.data_ptr(),
+                                        self.workspace.numel(), self.rank, self.world,
+                                        torch.cuda.current_stream(a.device).cuda_stream)
         check(rc, "oproj_allreduce")
         return out
 
