@@ -159,6 +159,10 @@ B200_API int32_t b200_decode_metadata(const int32_t* packed, int32_t batch, int3
  * stride ldo).
  * slots[r] / flags[r]: device arrays of every rank's buffers, mapped into this
  * process (e.g. CUDA symmetric memory): slots [2][world][slot_rows][N] bf16,
+ * ll_slots[r] (may be NULL): every rank's low-latency slots, uint32
+ * [2][world][ll_rows][N] zeroed once, used by split calls with M <= ll_rows
+ * (<= 128): each 8-byte word carries two bf16 values and the call's epoch, so
+ * readers poll the data itself instead of flags.  world <= 8.
  * flags uint32 [max_units * world + 2] zeroed once before the first call.  The
  * call's epoch lives in the flag words, so the launch may be captured in a
  * CUDA graph; every rank makes the same calls in the same order.  workspace:
@@ -172,6 +176,7 @@ B200_API int32_t b200_decode_metadata(const int32_t* packed, int32_t batch, int3
 B200_API int32_t b200_oproj_allreduce(void* out, int64_t ldo, const void* a, int64_t lda,
                              const void* w, int64_t ldw, int32_t M, int32_t N, int32_t K,
                              void* const* slots, int32_t slot_rows,
+                             uint32_t* const* ll_slots, int32_t ll_rows,
                              uint32_t* const* flags, int32_t max_units,
                              void* workspace, int64_t workspace_bytes,
                              int32_t rank, int32_t world, void* stream);

@@ -29,8 +29,8 @@ SIGNATURES = {
     "b200_varlen_prefill_error": (_I32, [_P, ctypes.POINTER(ctypes.c_int32)]),
     "b200_spec_accept_workspace_size": (_SZ, [_I32, _I32, _I32]),
     "b200_spec_accept": (_I32, [_P, _P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _P, _SZ, _P]),
-    "b200_oproj_allreduce": (_I32, [_P, _I64, _P, _I64, _P, _I64, _I32, _I32, _I32, _P, _I32, _P, _I32, _P, _I64,
-                                    _I32, _I32, _P]),
+    "b200_oproj_allreduce": (_I32, [_P, _I64, _P, _I64, _P, _I64, _I32, _I32, _I32, _P, _I32, _P, _I32, _P, _I32,
+                                    _P, _I64, _I32, _I32, _P]),
     "b200_oproj_allreduce_workspace_size": (_I64, []),
     "b200_oproj_allreduce_error": (_I32, [_P, ctypes.POINTER(ctypes.c_int32)]),
     "b200_decode_metadata": (_I32, [_P, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _P]),

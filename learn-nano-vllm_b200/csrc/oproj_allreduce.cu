@@ -24,6 +24,11 @@
 //   phase 2  for its rows, each CTA waits (bounded) for every rank's ready flag,
 //            sums the ranks' bf16 partials from LOCAL memory in fp32 in rank
 //            order (every rank gets the same bits) and writes bf16 y.
+// Low-latency slots (split calls with M <= ll_rows, i.e. decode batches): each
+// 8-byte word holds two bf16 values and the epoch, written with single 16-byte
+// stores (8-byte halves are single-copy atomic), and readers poll the words
+// themselves: no ready flags, no system-scope release or acquire on the path,
+// at twice the bytes over NVLink.
 // Phases 1 and 1b wait only on CTAs of this grid on this GPU (all resident: the
 // grid never exceeds the SM count and a CTA fills an SM), so phase 2's waits end.
 //
@@ -34,8 +39,10 @@
 // only after its own call e+1 ended, which waited for every rank's e+1 ready
 // flags; a rank publishes those only after its call e (its last read of that
 // parity) ended.  Unit 0 always has rows, so every call carries such a flag.
-// All epoch comparisons are wrap-safe.  Waits poll with one lane per flag, give
-// up after kWaitLimitNs and set the error word.  Flag words per rank (uint32,
+// Epoch 0 is skipped when the counter wraps (zeroed words never look current).
+// A peer may already have published the NEXT epoch into a ready flag (it ran
+// ahead by one call), never the one after.  Waits poll with one lane per flag,
+// give up after kWaitLimitNs and set the error word.  Flag words per rank (uint32,
 // zeroed once): [max_units][world] ready epochs, a finished-CTA counter, the
 // last epoch.
 #include "common.cuh"
@@ -55,9 +62,10 @@ struct Params {
     uint16_t* out;
     int64_t ldo;
     int32_t M, N, K, rank, world, tiles_n, splits, num_units, kb_count;
-    uint16_t* const* slots;  // [world] -> each rank's slots: [2][world][slot_rows][N] bf16
-    uint32_t* const* flags;  // [world] -> each rank's flag words
-    int32_t max_units, slot_rows;
+    uint16_t* const* slots;   // [world] -> each rank's slots: [2][world][slot_rows][N] bf16
+    uint32_t* const* ll;      // [world] -> each rank's low-latency slots [2][world][ll_rows][N/2] x (2 bf16, epoch)
+    uint32_t* const* flags;   // [world] -> each rank's flag words
+    int32_t max_units, slot_rows, ll_rows, use_ll;
     uint32_t* arrive;  // local [kArriveWords] split arrival epochs
     float* part;       // local [units][kBM][kBN] fp32 split partials
 };
@@ -101,18 +109,35 @@ __device__ __forceinline__ void bulk_store_wait(void* dst, const void* src, uint
     asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
-// v has reached `target` on a wrapping uint32 epoch counter
-__device__ __forceinline__ bool reached(uint32_t v, uint32_t target) { return int32_t(v - target) >= 0; }
+__device__ __forceinline__ uint32_t next_epoch(uint32_t e) { return e + 1u == 0u ? 2u : e + 1u; }
+// A ready flag shows epoch e: it holds e, or already the next epoch (its writer ran ahead by one
+// call).  Split arrival flags (this GPU, this grid) can only hold e or older.
+template <bool SYS>
+__device__ __forceinline__ bool shows(uint32_t v, uint32_t e) { return v == e || (SYS && v == next_epoch(e)); }
 
-// Whole warp: lane l < n waits until flags[l * stride] reaches epoch, all lanes in
-// parallel; true in every lane once all have, false in every lane on timeout.
+__device__ __forceinline__ uint4 ld_volatile_v4(const uint32_t* p) {
+    uint4 v;
+    asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p)
+                 : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_volatile_v4(uint32_t* p, uint4 v) {
+    asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+                 "r"(v.w)
+                 : "memory");
+}
+
+// Whole warp: lane l < n waits until flags[l * stride] shows epoch, all lanes in
+// parallel; true in every lane once all do, false in every lane on timeout.
 template <bool SYS>
 __device__ __forceinline__ bool warp_wait_flags(const uint32_t* flags, int stride, int n, uint32_t epoch) {
     const int lane = threadIdx.x & 31;
     auto ok = [&]() {
         if (lane >= n) return true;
         const uint32_t* f = flags + lane * stride;
-        return reached(SYS ? ld_acquire_sys(f) : ld_acquire_gpu(f), epoch);
+        return shows<SYS>(SYS ? ld_acquire_sys(f) : ld_acquire_gpu(f), epoch);
     };
     bool done = ok();
     if (__all_sync(0xffffffffu, done)) return true;
@@ -176,7 +201,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     uint32_t* my_flags = p.flags[p.rank];
     const int fl_count = p.max_units * p.world;  // finished-CTA counter, then the last epoch
-    const uint32_t epoch = __ldcg(my_flags + fl_count + 1) + 1u;
+    const uint32_t epoch = next_epoch(__ldcg(my_flags + fl_count + 1));
     const int parity = epoch & 1;
     const size_t slot_half = size_t(p.world) * p.slot_rows * p.N;
     // this rank's source region inside every rank's slot buffer
@@ -381,18 +406,82 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int sw = row & 7, c8 = k ^ (sw >> 1);
                 uint4 o = pack8(acc);
                 if (sw & 1) o = make_uint4(o.z, o.w, o.x, o.y);
-                const size_t off = push_off + size_t(ur.m0 + row) * p.N + ur.n0 + c8 * 8;
-                for (int r = 0; r < p.world; ++r) *reinterpret_cast<uint4*>(p.slots[r] + off) = o;
+                if (p.use_ll) {
+                    // 4 words (2 bf16 + epoch each) in two 16-byte stores; M <= ll_rows so m0 == 0
+                    const size_t w = (size_t(parity) * p.world + p.rank) * p.ll_rows * (p.N / 2) +
+                                     (size_t(row) * p.N + ur.n0 + c8 * 8) / 2;
+                    const uint4 w0 = make_uint4(o.x, epoch, o.y, epoch), w1 = make_uint4(o.z, epoch, o.w, epoch);
+                    for (int r = 0; r < p.world; ++r) {
+                        st_volatile_v4(p.ll[r] + 2 * w, w0);
+                        st_volatile_v4(p.ll[r] + 2 * w + 4, w1);
+                    }
+                } else {
+                    const size_t off = push_off + size_t(ur.m0 + row) * p.N + ur.n0 + c8 * 8;
+                    for (int r = 0; r < p.world; ++r) *reinterpret_cast<uint4*>(p.slots[r] + off) = o;
+                }
             }
         }
         __syncthreads();
-        if (go && !failed() && tid < p.world) st_release_sys(p.flags[tid] + u * p.world + p.rank, epoch);
+        if (go && !p.use_ll && !failed() && tid < p.world)
+            st_release_sys(p.flags[tid] + u * p.world + p.rank, epoch);
     }
 
     // ------------------------------------------------------------------ phase 2
     const uint16_t* local = p.slots[p.rank] + size_t(parity) * slot_half;
     const size_t src_stride = size_t(p.slot_rows) * p.N;
-    for (int u = blockIdx.x; u < p.num_units; u += gridDim.x) {
+    if (p.use_ll) {
+        // one unit per CTA (split); poll this CTA's rows' words from every rank, sum in rank order
+        const UnitRows ur = unit_rows(p, blockIdx.x);
+        const uint32_t* ll_local = p.ll[p.rank] + size_t(parity) * p.world * p.ll_rows * p.N;
+        const size_t src_words = size_t(p.ll_rows) * (p.N / 2);
+        const int items = (ur.r1 - ur.r0) * (kBN / 8);
+        constexpr int kMaxWorld = 8;
+        for (int i = tid; i < items && !failed(); i += kThreads) {
+            const int row = ur.r0 + i / (kBN / 8), c8 = i % (kBN / 8);
+            const size_t w = (size_t(row) * p.N + ur.n0 + c8 * 8) / 2;
+            uint4 v0[kMaxWorld], v1[kMaxWorld];
+            bool all = true;
+#pragma unroll
+            for (int r = 0; r < kMaxWorld; ++r)
+                if (r < p.world) {
+                    v0[r] = ld_volatile_v4(ll_local + 2 * (r * src_words + w));
+                    v1[r] = ld_volatile_v4(ll_local + 2 * (r * src_words + w) + 4);
+                    all = all && v0[r].y == epoch && v0[r].w == epoch && v1[r].y == epoch && v1[r].w == epoch;
+                }
+            if (!all) {
+                const uint64_t t0 = global_timer_ns();
+                while (!all) {
+                    all = true;
+#pragma unroll
+                    for (int r = 0; r < kMaxWorld; ++r)
+                        if (r < p.world && !(v0[r].y == epoch && v0[r].w == epoch && v1[r].y == epoch &&
+                                             v1[r].w == epoch)) {
+                            v0[r] = ld_volatile_v4(ll_local + 2 * (r * src_words + w));
+                            v1[r] = ld_volatile_v4(ll_local + 2 * (r * src_words + w) + 4);
+                            all = all && v0[r].y == epoch && v0[r].w == epoch && v1[r].y == epoch &&
+                                  v1[r].w == epoch;
+                        }
+                    if (!all && global_timer_ns() - t0 > kWaitLimitNs) {
+                        flag_error(sm, 16);
+                        break;
+                    }
+                }
+            }
+            float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int r = 0; r < kMaxWorld; ++r)
+                if (r < p.world) {
+                    const uint32_t d[4] = {v0[r].x, v0[r].z, v1[r].x, v1[r].z};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        acc[2 * e] += __uint_as_float(d[e] << 16);
+                        acc[2 * e + 1] += __uint_as_float(d[e] & 0xFFFF0000u);
+                    }
+                }
+            *reinterpret_cast<uint4*>(p.out + int64_t(row) * p.ldo + ur.n0 + c8 * 8) = pack8(acc);
+        }
+    }
+    for (int u = blockIdx.x; u < p.num_units && !p.use_ll; u += gridDim.x) {
         const UnitRows ur = unit_rows(p, u);
         if (ur.r0 >= ur.r1) continue;
         if (warp == 0) {
@@ -462,7 +551,8 @@ extern "C" int64_t b200_oproj_allreduce_workspace_size(void) {
 
 extern "C" int32_t b200_oproj_allreduce(void* out, int64_t ldo, const void* a, int64_t lda, const void* w,
                                         int64_t ldw, int32_t M, int32_t N, int32_t K, void* const* slots,
-                                        int32_t slot_rows, uint32_t* const* flags, int32_t max_units,
+                                        int32_t slot_rows, uint32_t* const* ll_slots, int32_t ll_rows,
+                                        uint32_t* const* flags, int32_t max_units,
                                         void* workspace, int64_t workspace_bytes, int32_t rank, int32_t world,
                                         void* stream) {
     using namespace b200;
@@ -471,7 +561,8 @@ extern "C" int32_t b200_oproj_allreduce(void* out, int64_t ldo, const void* a, i
     B200_REQUIRE(M >= 0 && N > 0 && K > 0, "oproj_allreduce: M %d N %d K %d", M, N, K);
     if (M == 0) return B200_OK;
     B200_REQUIRE(out && a && w && slots && flags, "oproj_allreduce: null pointer");
-    B200_REQUIRE(world >= 1 && rank >= 0 && rank < world, "oproj_allreduce: rank %d of %d", rank, world);
+    B200_REQUIRE(world >= 1 && world <= 8 && rank >= 0 && rank < world, "oproj_allreduce: rank %d of %d", rank,
+                 world);
     if (N % kBN != 0 || K % kBK != 0)
         return fail(B200_ERR_UNSUPPORTED, "oproj_allreduce: N %% 256 and K %% 64 must be 0 (N %d, K %d)", N, K);
     B200_REQUIRE(ldo >= N && lda >= K && ldw >= K && ldo % 8 == 0, "oproj_allreduce: strides");
@@ -512,6 +603,9 @@ extern "C" int32_t b200_oproj_allreduce(void* out, int64_t ldo, const void* a, i
     p.flags = flags;
     p.max_units = max_units;
     p.slot_rows = slot_rows;
+    p.ll = ll_slots;
+    p.ll_rows = ll_rows;
+    p.use_ll = splits > 1 && ll_slots != nullptr && M <= ll_rows && M <= kBM;
     p.arrive = static_cast<uint32_t*>(workspace);
     p.part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kArriveWords * 4);
     const int smem = int(sizeof(Smem)) + 1024;

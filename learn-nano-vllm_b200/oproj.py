@@ -22,7 +22,7 @@ _BN = 256
 
 class OprojAllReduce:
 
-    def __init__(self, group, max_tokens: int, hidden: int, device=None):
+    def __init__(self, group, max_tokens: int, hidden: int, device=None, low_latency: bool = True):
         import torch.distributed._symmetric_memory as symm_mem
         self.group = group
         self.rank = dist.get_rank(group)
@@ -36,14 +36,21 @@ class OprojAllReduce:
         self.slots = symm_mem.empty(2 * self.world * max_tokens * hidden, dtype=torch.bfloat16, device=self.device)
         self.flags = symm_mem.empty(self.max_units * self.world + 2, dtype=torch.int32, device=self.device)
         self.flags.zero_()
+        # low-latency slots for decode batches (M <= 128): words of (2 bf16, epoch)
+        self.ll_rows = min(128, max_tokens) if low_latency else 0
+        self.ll = symm_mem.empty(max(2 * self.world * self.ll_rows * hidden, 4), dtype=torch.int32, device=self.device)
+        self.ll.zero_()
         h_slots = symm_mem.rendezvous(self.slots, group)
         h_flags = symm_mem.rendezvous(self.flags, group)
+        h_ll = symm_mem.rendezvous(self.ll, group)
         # device arrays of every rank's buffer addresses (this tensor's offset inside each mapping)
         ds = self.slots.data_ptr() - h_slots.buffer_ptrs[self.rank]
         df = self.flags.data_ptr() - h_flags.buffer_ptrs[self.rank]
         self.slot_ptrs = torch.tensor([b + ds for b in h_slots.buffer_ptrs], dtype=torch.int64, device=self.device)
         self.flag_ptrs = torch.tensor([b + df for b in h_flags.buffer_ptrs], dtype=torch.int64, device=self.device)
-        self._handles = (h_slots, h_flags)
+        dl = self.ll.data_ptr() - h_ll.buffer_ptrs[self.rank]
+        self.ll_ptrs = torch.tensor([b + dl for b in h_ll.buffer_ptrs], dtype=torch.int64, device=self.device)
+        self._handles = (h_slots, h_flags, h_ll)
         self.workspace = torch.zeros(lib().b200_oproj_allreduce_workspace_size(), dtype=torch.uint8,
                                      device=self.device)
         self.calls = 0
@@ -61,7 +68,7 @@ class OprojAllReduce:
         self.calls += 1
         rc = lib().b200_oproj_allreduce(out.data_ptr(), out.stride(0), a.data_ptr(), a.stride(0), w.data_ptr(),
                                         w.stride(0), M, N, K, self.slot_ptrs.data_ptr(), self.max_tokens,
-                                        self.flag_ptrs.data_ptr(), self.max_units, self.workspace.data_ptr(),
+                                        self.ll_ptrs.data_ptr(), self.ll_rows, self.flag_ptrs.data_ptr(), self.max_units, self.workspace.data_ptr(),
                                         self.workspace.numel(), self.rank, self.world,
                                         torch.cuda.current_stream(a.device).cuda_stream)
         check(rc, "oproj_allreduce")
