@@ -6,6 +6,11 @@ no padded nested lists), copies it to the device in one transfer and expands it 
 with b200_decode_metadata.  It returns the tensors prepare_decode / prepare_sample
 return: input_ids, positions (int64), slot_mapping, context_lens, block_tables
 (int32, -1 padded to the batch's longest table) and temperatures (fp32).
+
+Tensor-parallel worker ranks receive trimmed sequences (Sequence.__getstate__,
+nanovllm/engine/sequence.py:72-83, carries no temperature) and never sample
+(model_runner.py:216 reads temperatures on rank 0 only): they build with
+temperatures=False, which writes 1.0 instead of reading them.
 """
 import itertools
 
@@ -37,20 +42,38 @@ class DecodeMetadata:
             ev.synchronize()  # the copy that last read this buffer has finished
         return self._host[self._flip]
 
-    def build(self, seqs, block_size):
+    @staticmethod
+    def packed_size(seqs):
+        """(int32 words of the packed buffer, block-table width W) for a batch."""
+        nblk = sum(len(s.block_table) for s in seqs)
+        W = max(max((len(s.block_table) for s in seqs), default=1), 1)
+        return 4 * len(seqs) + 1 + nblk, W
+
+    @staticmethod
+    def pack(seqs, h, temperatures=True):
+        """Write the packed buffer into the int32 numpy array h: [B] lengths, [B] last tokens,
+        [B] temperatures (fp32 bits; 1.0 when temperatures is False), [B + 1] block-list
+        offsets, then every block id."""
         B = len(seqs)
         tables = [s.block_table for s in seqs]
         nblk = np.fromiter((len(t) for t in tables), np.int32, B)
-        W = max(int(nblk.max()), 1)
         n = 4 * B + 1 + int(nblk.sum())
-        host = self._staging(n)
-        h = host.numpy()
         h[:B] = np.fromiter((len(s) for s in seqs), np.int32, B)
         h[B:2 * B] = np.fromiter((s.last_token for s in seqs), np.int32, B)
-        h[2 * B:3 * B] = np.fromiter((s.temperature for s in seqs), np.float32, B).view(np.int32)
+        if temperatures:
+            h[2 * B:3 * B] = np.fromiter((s.temperature for s in seqs), np.float32, B).view(np.int32)
+        else:
+            h[2 * B:3 * B] = np.float32(1.0).view(np.int32)
         h[3 * B] = 0
         np.cumsum(nblk, out=h[3 * B + 1:4 * B + 1])
         h[4 * B + 1:n] = np.fromiter(itertools.chain.from_iterable(tables), np.int32, n - 4 * B - 1)
+        return n
+
+    def build(self, seqs, block_size, temperatures=True):
+        B = len(seqs)
+        n, W = self.packed_size(seqs)
+        host = self._staging(n)
+        self.pack(seqs, host.numpy(), temperatures)
         stream = torch.cuda.current_stream(self.device)
         packed = torch.empty(n, dtype=torch.int32, device=self.device)
         packed.copy_(host[:n], non_blocking=True)

@@ -40,7 +40,9 @@ def _device_prepare_decode(self, seqs):
     meta = self.__dict__.get("_b200_meta")
     if meta is None:
         meta = self._b200_meta = DecodeMetadata()
-    input_ids, positions, slot_mapping, context_lens, block_tables, temps = meta.build(seqs, self.block_size)
+    # worker ranks get trimmed sequences without temperatures and do not sample
+    input_ids, positions, slot_mapping, context_lens, block_tables, temps = meta.build(
+        seqs, self.block_size, temperatures=self.rank == 0)
     set_context(False, slot_mapping=slot_mapping, context_lens=context_lens, block_tables=block_tables)
     self._b200_temps = (seqs, temps)
     return input_ids, positions
@@ -53,6 +55,38 @@ def _device_prepare_sample(self, seqs):
     if cached is not None and cached[0] is seqs:
         return cached[1]
     return _ORIGINAL_PREPARE[1](self, seqs)
+
+
+class _RowParallelState:
+    """The fused GEMM + all-reduce buffers of this process, one per (output size, device),
+    shared by every RowParallelLinear (they run one after another on one stream)."""
+    ops = {}
+    max_tokens = 16384  # nano-vLLM's default max_num_batched_tokens; larger batches use the stock path
+
+    @classmethod
+    def get(cls, n, device):
+        key = (n, device)
+        op = cls.ops.get(key)
+        if op is None:
+            import torch.distributed as dist
+            from .oproj import OprojAllReduce
+            op = cls.ops[key] = OprojAllReduce(dist.group.WORLD, max_tokens=cls.max_tokens, hidden=n, device=device)
+        return op
+
+
+_ORIGINAL_ROW = []
+
+
+def _fused_row_parallel_forward(self, x):
+    """RowParallelLinear.forward (nanovllm/layers/linear.py:152-156): this rank's F.linear and
+    the all-reduce over the tensor-parallel ranks as one kernel (oproj.OprojAllReduce), for
+    bias-free bf16 layers with N % 256 == 0 and K % 64 == 0.  Every rank sees the same batch,
+    so every rank takes the same branch (the kernel is collective)."""
+    n, k = self.weight.shape
+    if (self.tp_size == 1 or self.bias is not None or x.dtype != torch.bfloat16 or x.dim() != 2
+            or n % 256 or k % 64 or x.shape[0] > _RowParallelState.max_tokens or x.stride(-1) != 1):
+        return _ORIGINAL_ROW[0](self, x)
+    return _RowParallelState.get(n, x.device)(x, self.weight)
 
 
 class _FusedSamplerState:
@@ -70,7 +104,7 @@ def _fused_sampler_forward(self, logits, temperatures):
 
 
 def install(fuse_qk_epilogue: bool = False, fuse_sampler: bool = False, workers: bool = False,
-            worker_setup: tuple = (), device_metadata: bool = False):
+            worker_setup: tuple = (), device_metadata: bool = False, fuse_row_parallel: bool = False):
     """Patch the importable `nanovllm` package; returns the patched modules.
 
     With fuse_qk_epilogue, Qwen3Attention.forward also runs q/k RMSNorm, RoPE and
@@ -79,7 +113,9 @@ def install(fuse_qk_epilogue: bool = False, fuse_sampler: bool = False, workers:
     fuse_sampler, Sampler.forward becomes the one-pass fused sampler (ops.sample;
     its noise stream is seeded from torch.initial_seed()).  With device_metadata,
     ModelRunner.prepare_decode / prepare_sample build the decode step's tensors on
-    the device from one packed host-to-device copy (decode_meta).  With workers, the
+    the device from one packed host-to-device copy (decode_meta).  With
+    fuse_row_parallel, RowParallelLinear.forward (o_proj, down_proj) runs its GEMM and
+    the tensor-parallel all-reduce as one kernel over peer memory (oproj).  With workers, the
     engine's tensor-parallel ranks (spawned processes, nanovllm/engine/llm_engine.py:24-30)
     run install() with the same options before building their ModelRunner;
     worker_setup lists "module:function" hooks they run first.
@@ -106,12 +142,16 @@ def install(fuse_qk_epilogue: bool = False, fuse_sampler: bool = False, workers:
         _ORIGINAL_PREPARE.extend([runner_mod.ModelRunner.prepare_decode, runner_mod.ModelRunner.prepare_sample])
     runner_mod.ModelRunner.prepare_decode = _device_prepare_decode if device_metadata else _ORIGINAL_PREPARE[0]
     runner_mod.ModelRunner.prepare_sample = _device_prepare_sample if device_metadata else _ORIGINAL_PREPARE[1]
+    linear_mod = importlib.import_module("nanovllm.layers.linear")
+    if not _ORIGINAL_ROW:
+        _ORIGINAL_ROW.append(linear_mod.RowParallelLinear.forward)
+    linear_mod.RowParallelLinear.forward = _fused_row_parallel_forward if fuse_row_parallel else _ORIGINAL_ROW[0]
     if workers:
         import functools
         entry = importlib.import_module("__graft_entry__")
         opts = {"setup": list(worker_setup),
                 "install": {"fuse_qk_epilogue": fuse_qk_epilogue, "fuse_sampler": fuse_sampler,
-                            "device_metadata": device_metadata}}
+                            "device_metadata": device_metadata, "fuse_row_parallel": fuse_row_parallel}}
         engine_mod.ModelRunner = functools.partial(entry.nanovllm_worker, options=opts)
     else:
         engine_mod.ModelRunner = runner_mod.ModelRunner

@@ -15,6 +15,38 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 sys.path.insert(0, ROOT)
 
 
+def check_row_parallel(pkg, rank, world, dev):
+    """install(fuse_row_parallel=True) on the reference's own RowParallelLinear
+    (nanovllm/layers/linear.py:130-156): the patched forward against the stock one
+    (F.linear + NCCL all-reduce), when the reference is installed in baseline/_ref."""
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "nanovllm")):
+        return 0.0
+    sys.path.insert(0, ref)
+    from nanovllm.layers import linear
+    pkg.install(fuse_row_parallel=True)
+    fused = linear.RowParallelLinear.forward
+    stock = pkg.integrate._ORIGINAL_ROW[0]
+    torch.manual_seed(99)  # same weights on every rank
+    with torch.device(dev):
+        layer = linear.RowParallelLinear(2048, 1024, bias=False).to(torch.bfloat16)
+    full = (torch.randn(1024, 2048, device=dev) * 0.03).to(torch.bfloat16)
+    layer.weight_loader(layer.weight, full)
+    worst = 0.0
+    for M in (64, 700, 3):
+        x_full = torch.randn(M, 2048, device=dev).to(torch.bfloat16)
+        x = x_full.chunk(world, dim=1)[rank].contiguous()
+        y = fused(layer, x)
+        y_ref = stock(layer, x)
+        torch.cuda.synchronize()
+        d = (y.float() - y_ref.float()).abs().max().item() / y_ref.float().abs().max().item()
+        assert d <= 2 ** -6, ("row-parallel", M, d)
+        worst = max(worst, d)
+    pkg.install()  # stock RowParallelLinear again
+    assert linear.RowParallelLinear.forward is stock
+    return worst
+
+
 def main():
     rank, world, port = int(sys.argv[1]), int(sys.argv[2]), int(sys.argv[3])
     import __graft_entry__
@@ -78,6 +110,7 @@ def main():
         del graph
         assert op.error() == 0, "a bounded wait gave up"
         calls += op.calls
+    worst = max(worst, check_row_parallel(pkg, rank, world, dev))
     print(json.dumps({"rank": rank, "world": world, "calls": calls, "worst_rel": worst}), flush=True)
     dist.destroy_process_group()
 
