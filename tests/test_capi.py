@@ -70,3 +70,31 @@ def test_python_wrapper_asserts_like_reference(pkg):
         pkg.store_kvcache(key, key, cache, cache, torch.zeros(3, dtype=torch.int32))   # numel != N
     with pytest.raises(AssertionError):
         pkg.store_kvcache(key, key, cache, cache, torch.zeros(4, dtype=torch.int32))   # CPU tensors
+
+
+def test_oproj_allreduce_argument_errors(pkg):
+    """b200_oproj_allreduce rejects bad shapes, ranks and pointers before any CUDA call."""
+    lib = pkg.lib()
+    d = ctypes.c_void_p(256)
+
+    def call(M=64, N=1024, K=512, ldo=1024, out=d, rank=0, world=2):
+        return lib.b200_oproj_allreduce(out, ldo, d, K, d, K, M, N, K, d, 512, d, 128, d, 148, d, 1 << 20,
+                                        rank, world, None)
+    assert call(M=0) == 0                                   # nothing to do, no launch
+    assert call(M=-1) == 1
+    assert call(out=None) == 1 and b"null" in lib.b200_last_error()
+    assert call(rank=2) == 1 and b"rank" in lib.b200_last_error()
+    assert call(world=9) == 1
+    assert call(N=300) == 2 and b"256" in lib.b200_last_error()
+    assert call(K=100) == 2
+    assert call(ldo=100) == 1 and b"strides" in lib.b200_last_error()
+    assert lib.b200_oproj_allreduce_error(None, None) == 1
+
+
+def test_decode_metadata_argument_errors(pkg):
+    lib = pkg.lib()
+    d = ctypes.c_void_p(256)
+    assert lib.b200_decode_metadata(d, 0, 4, 256, d, d, d, d, d, d, None) == 0   # empty batch
+    assert lib.b200_decode_metadata(d, -1, 4, 256, d, d, d, d, d, d, None) == 1
+    assert lib.b200_decode_metadata(d, 4, 0, 256, d, d, d, d, d, d, None) == 1
+    assert lib.b200_decode_metadata(None, 4, 4, 256, d, d, d, d, d, d, None) == 1
