@@ -14,7 +14,9 @@ Public API
   sample                    fused temperature + exponential-race sampler
   DecodeMetadata            decode-step metadata built on the device
   OprojAllReduce            tensor-parallel o_proj GEMM fused with its all-reduce over peer memory
-  install                   patch nano-vLLM to use this package's Attention
+  install                   patch nano-vLLM to use this package's Attention (options: the fused
+                            q/k epilogue, sampler, device decode metadata, row-parallel
+                            GEMM + all-reduce, tensor-parallel worker processes)
   context                   mirror of nanovllm.utils.context
 """
 from . import context, ops
@@ -26,6 +28,6 @@ from .integrate import install
 from .ops import (flash_attn_varlen_func, flash_attn_with_kvcache, paged_attention, paged_workspace,
                   qk_norm_rope_store, sample, spec_accept, store_kvcache, workspace_error)
 
-__all__ = ["Attention", "B200Error", "DecodeMetadata", "OprojAllReduce", "context", "flash_attn_varlen_func", "flash_attn_with_kvcache", "install",
-           "lib", "paged_attention", "paged_workspace", "qk_norm_rope_store", "sample", "spec_accept",
-           "store_kvcache", "workspace_error"]
+__all__ = ["Attention", "B200Error", "DecodeMetadata", "OprojAllReduce", "context", "flash_attn_varlen_func",
+           "flash_attn_with_kvcache", "install", "lib", "paged_attention", "paged_workspace", "qk_norm_rope_store",
+           "sample", "spec_accept", "store_kvcache", "workspace_error"]
