@@ -14,3 +14,34 @@ def test_slots_positions_and_padding():
     assert lens.tolist() == [1, 256, 257, 600]
     assert bt.shape == (4, 3) and bt[0].tolist() == [7, -1, -1] and bt[3].tolist() == [1, 2, 5]
     assert np.allclose(temps, [0.6, 1.0, 0.5, 1.2])
+
+
+def _golden():
+    import os
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "decode_meta.npz")
+    return np.load(path)
+
+
+def _cases(g):
+    return sorted({k.split(".")[0] for k in g.files})
+
+
+def test_oracle_matches_reference_builders():
+    """Pinned to the reference's own prepare_decode / prepare_sample outputs
+    (tests/golden/decode_meta.npz, generator beside it): every tensor equal."""
+    g = _golden()
+    names = _cases(g)
+    assert names == ["b1", "b17_short", "b256_long", "b64_mixed"]
+    for name in names:
+        off = g[name + ".table_offsets"]
+        flat = g[name + ".tables_flat"]
+        seqs = [(int(n), int(t), float(tp), flat[off[i]:off[i + 1]].tolist())
+                for i, (n, t, tp) in enumerate(zip(g[name + ".lengths"], g[name + ".last_tokens"],
+                                                   g[name + ".temperatures_in"]))]
+        ids, pos, slots, lens, bt, temps = decode_metadata_ref(seqs, 256)
+        assert np.array_equal(ids, g[name + ".input_ids"]), name
+        assert np.array_equal(pos, g[name + ".positions"]), name
+        assert np.array_equal(slots, g[name + ".slot_mapping"]) and slots.dtype == g[name + ".slot_mapping"].dtype
+        assert np.array_equal(lens, g[name + ".context_lens"]), name
+        assert np.array_equal(bt, g[name + ".block_tables"]), name
+        assert np.array_equal(temps, g[name + ".temperatures"]) and temps.dtype == np.float32, name

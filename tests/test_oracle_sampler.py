@@ -42,3 +42,19 @@ def test_generator_path_distribution():
     toks = so.sample_ref(x, np.ones(rows, np.float32), seed=11, offset=0)
     freq = np.bincount(toks, minlength=V)[:8] / rows
     assert np.abs(freq - p).max() < 0.03
+
+
+def test_reference_formula_matches_reference_sampler():
+    """Pinned to the reference Sampler's own tokens on its own Exp(1) draw
+    (tests/golden/sampler.npz, generator beside it)."""
+    import os
+    g = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "sampler.npz"))
+    names = sorted({k.split(".")[0] for k in g.files})
+    assert len(names) == 3
+    for name in names:
+        x, t, e, want = (g[name + s] for s in (".logits", ".temperatures", ".noise", ".tokens"))
+        got = so.reference_formula(x, t, e)
+        assert np.array_equal(got, want), (name, np.flatnonzero(got != want))
+        # the one-pass score (x/T - ln E) is the same argmax up to float near-ties
+        fused = np.argmax(so.fused_scores(x, t, e), axis=1)
+        assert (fused == want).mean() >= 0.95, name
