@@ -80,11 +80,13 @@ _ORIGINAL_ROW = []
 def _fused_row_parallel_forward(self, x):
     """RowParallelLinear.forward (nanovllm/layers/linear.py:152-156): this rank's F.linear and
     the all-reduce over the tensor-parallel ranks as one kernel (oproj.OprojAllReduce), for
-    bias-free bf16 layers with N % 256 == 0 and K % 64 == 0.  Every rank sees the same batch,
-    so every rank takes the same branch (the kernel is collective)."""
+    bias-free bf16 layers with N % 256 == 0 and K % 64 == 0 and activations the kernel's tensor
+    maps can address (unit inner stride, 16-byte aligned rows).  Every rank sees the same batch
+    and the same layer shapes, so every rank takes the same branch (the kernel is collective)."""
     n, k = self.weight.shape
     if (self.tp_size == 1 or self.bias is not None or x.dtype != torch.bfloat16 or x.dim() != 2
-            or n % 256 or k % 64 or x.shape[0] > _RowParallelState.max_tokens or x.stride(-1) != 1):
+            or n % 256 or k % 64 or x.shape[0] > _RowParallelState.max_tokens or x.stride(-1) != 1
+            or x.stride(0) % 8 or x.data_ptr() % 16):
         return _ORIGINAL_ROW[0](self, x)
     return _RowParallelState.get(n, x.device)(x, self.weight)
 
@@ -115,7 +117,8 @@ def install(fuse_qk_epilogue: bool = False, fuse_sampler: bool = False, workers:
     ModelRunner.prepare_decode / prepare_sample build the decode step's tensors on
     the device from one packed host-to-device copy (decode_meta).  With
     fuse_row_parallel, RowParallelLinear.forward (o_proj, down_proj) runs its GEMM and
-    the tensor-parallel all-reduce as one kernel over peer memory (oproj).  With workers, the
+    the tensor-parallel all-reduce as one kernel over peer memory (oproj); every rank must run
+    it, so it implies workers.  With workers, the
     engine's tensor-parallel ranks (spawned processes, nanovllm/engine/llm_engine.py:24-30)
     run install() with the same options before building their ModelRunner;
     worker_setup lists "module:function" hooks they run first.
@@ -146,7 +149,7 @@ def install(fuse_qk_epilogue: bool = False, fuse_sampler: bool = False, workers:
     if not _ORIGINAL_ROW:
         _ORIGINAL_ROW.append(linear_mod.RowParallelLinear.forward)
     linear_mod.RowParallelLinear.forward = _fused_row_parallel_forward if fuse_row_parallel else _ORIGINAL_ROW[0]
-    if workers:
+    if workers or fuse_row_parallel:
         import functools
         entry = importlib.import_module("__graft_entry__")
         opts = {"setup": list(worker_setup),

@@ -70,6 +70,9 @@ def _worker(rank, world, port, ret):
         results.append(("bf16 2-D", run(x), (1, True)))
         results.append(("fp32 input", run(x.float().contiguous(), _fp32_copy(layer, linear)), (0, True)))
         results.append(("non-unit inner stride", run(x_full[:, rank::world]), (0, True)))
+        wide = torch.randn(40, 256 // world + 4).to(torch.bfloat16)
+        results.append(("rows not 16-byte aligned", run(wide[:, :256 // world]), (0, True)))
+        results.append(("base not 16-byte aligned", run(wide[:, 1:1 + 256 // world]), (0, True)))
         old = integrate._RowParallelState.max_tokens
         integrate._RowParallelState.max_tokens = 39
         results.append(("M above the buffers", run(x), (0, True)))
@@ -79,6 +82,7 @@ def _worker(rank, world, port, ret):
         with_bias.bias.data.normal_()
         results.append(("bias", run(x, with_bias), (0, True)))
         odd = linear.RowParallelLinear(256, 320, bias=False).to(torch.bfloat16)
+        odd.weight.data.normal_()
         results.append(("N % 256 != 0", run(x, odd), (0, True)))
         layer.tp_size = 1
         results.append(("tp_size 1", run(x), (0, True)))
