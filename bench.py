@@ -673,6 +673,47 @@ def _engine_worker_setup():
     mr.load_model = _random_init
 
 
+def engine_watchdog(target, period=0.5):
+    """Stop within a second when a tensor-parallel engine worker dies: rank 0 would otherwise
+    wait in its next collective until the process group's timeout.  Workers are the child
+    processes spawned with `target` (nano-vLLM's llm_engine.ModelRunner, llm_engine.py:24-30);
+    other children (compile pools) are ignored.  Kills the remaining workers, prints one JSON
+    error line, exits 3.  Returns an event that stops the watch (set it once the measured work
+    is done, before shutdown)."""
+    import threading
+    from multiprocessing import context as mp_context
+    workers = []
+    stop = threading.Event()
+    start = mp_context.SpawnProcess.start
+
+    def start_and_record(proc):
+        # the target is only readable before start() (which drops it)
+        if getattr(proc, "_target", None) is target:
+            workers.append(proc)
+        return start(proc)
+
+    mp_context.SpawnProcess.start = start_and_record
+
+    def loop():
+        while not stop.is_set():
+            for proc in list(workers):
+                code = proc.exitcode
+                if code is None:
+                    continue
+                if code != 0:
+                    print(json.dumps({"error": f"engine worker pid {proc.pid} exited with code {code}"}),
+                          flush=True)
+                    for other in workers:
+                        if other.exitcode is None:
+                            other.kill()
+                    os._exit(3)
+                workers.remove(proc)
+            stop.wait(period)
+
+    threading.Thread(target=loop, name="engine-watchdog", daemon=True).start()
+    return stop
+
+
 def run_engine(args, pkg):
     """Config 2 through nano-vLLM's own LLM engine (scheduler, block manager,
     prefix cache, CUDA-graph decode): 256 requests, prompt and output lengths
@@ -694,6 +735,8 @@ def run_engine(args, pkg):
         import __graft_entry__ as entry
         le.ModelRunner = functools.partial(entry.nanovllm_worker_stock, setup=("bench:_engine_worker_setup",))
     from nanovllm import LLM, SamplingParams
+    import nanovllm.engine.llm_engine as le
+    watch = engine_watchdog(le.ModelRunner) if tp > 1 else None
     path = _qwen3_config_dir(args.engine_model)
     t_init = time.perf_counter()
     llm = LLM(path, enforce_eager=False, max_model_len=4096, gpu_memory_utilization=args.gpu_mem,
@@ -711,6 +754,8 @@ def run_engine(args, pkg):
         t = time.perf_counter()
         out = llm.generate(prompts, sps, use_tqdm=False)
         t = time.perf_counter() - t
+    if watch is not None:
+        watch.set()  # measured work done: worker exits during shutdown are not failures of the run
     total = sum(sp.max_tokens for sp in sps)
     assert all(len(o["token_ids"]) == sp.max_tokens for o, sp in zip(out, sps))
     print(json.dumps({
