@@ -52,7 +52,9 @@ enum b200_dtype { B200_F16 = 0, B200_BF16 = 1, B200_F32 = 2 };
 /* Message of the last failed call on this host thread ("" if none). */
 B200_API const char* b200_last_error(void);
 
-/* Bumped whenever a signature below changes. */
+/* Bumped whenever a signature below changes (2: b200_oproj_allreduce takes its
+ * split-K workspace and low-latency slots; the epoch moved to the device). */
+#define B200_ABI_VERSION 2
 B200_API int32_t b200_abi_version(void);
 
 /*

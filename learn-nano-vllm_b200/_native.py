@@ -40,7 +40,7 @@ SIGNATURES = {
     "b200_qk_norm_rope_store": (_I32, [_P, _I64, _P, _I64, _P, _I64, _P, _P, _P, _F, _P, _I32, _P, _P, _P, _I64,
                                        _I32, _I32, _I32, _I32, _I32, _P]),
 }
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 _lib = None
 _lock = threading.Lock()

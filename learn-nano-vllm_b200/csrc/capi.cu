@@ -81,7 +81,7 @@ extern "C" {
 
 const char* b200_last_error(void) { return b200::g_last_error; }
 
-int32_t b200_abi_version(void) { return 1; }
+int32_t b200_abi_version(void) { return B200_ABI_VERSION; }
 
 int32_t b200_workspace_error(const void* workspace, void* stream, int32_t* flag) {
     B200_REQUIRE(workspace != nullptr && flag != nullptr, "workspace_error: null pointer");
