@@ -6,8 +6,8 @@ Sequence objects (nanovllm/engine/sequence.py) with seeded lengths, last tokens,
 temperatures and block tables.  The builders' pinned-memory host tensors and
 .cuda() copies are made no-ops for the run (there is no GPU here); nothing else is
 changed.  Records every sequence's inputs and the tensors the builders returned or
-put in the context.  Needs the reference checkout (default /root/reference, or
-argv[1]); run once in the development container, output committed.
+put in the context.  Needs the reference checkout (its directory as argv[1] or in
+NANOVLLM_REF); run once in the development container, output committed.
 
 Usage:  python tests/golden/gen_decode_meta_golden.py [REF_DIR]
 """
@@ -18,7 +18,9 @@ os.environ.setdefault("TORCH_COMPILE_DISABLE", "1")
 import numpy as np
 import torch
 
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("NANOVLLM_REF", "")
+if not os.path.isdir(os.path.join(REF, "nanovllm")):
+    sys.exit(__doc__)
 sys.path.insert(0, REF)
 from nanovllm.engine import model_runner  # noqa: E402
 from nanovllm.engine.sequence import Sequence  # noqa: E402

@@ -5,8 +5,8 @@ RotaryEmbedding.forward (nanovllm/layers/rotary_embedding.py:37-48) eagerly on
 CPU (torch.compile disabled) in the order of Qwen3Attention.forward
 (nanovllm/models/qwen3.py:79-85): split of the fused QKV output, q_norm /
 k_norm, rotary embedding.  Records the inputs (as raw bits), the module's
-cos_sin_cache and the q / k it produced.  Needs the reference checkout
-(default /root/reference, or argv[1]); it is run once in the development
+cos_sin_cache and the q / k it produced.  Needs the reference checkout (its
+directory as argv[1] or in NANOVLLM_REF); it is run once in the development
 container and its output is committed.  The GPU box never runs it.
 
 Usage:  python tests/golden/gen_qk_norm_rope_golden.py [REF_DIR]
@@ -18,7 +18,9 @@ os.environ.setdefault("TORCH_COMPILE_DISABLE", "1")
 import numpy as np
 import torch
 
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("NANOVLLM_REF", "")
+if not os.path.isdir(os.path.join(REF, "nanovllm")):
+    sys.exit(__doc__)
 sys.path.insert(0, REF)
 from nanovllm.layers.layernorm import RMSNorm  # noqa: E402
 from nanovllm.layers.rotary_embedding import RotaryEmbedding  # noqa: E402

@@ -5,8 +5,9 @@ Runs nano-vLLM's Sampler.forward (nanovllm/layers/sampler.py:7-12) eagerly on CP
 Exp(1) noise with torch's CPU generator right after the seed is set (nothing else in
 forward draws), so replaying the seed recovers the exact noise tensor; it is
 recorded with the tokens, after checking that the reference formula on it gives
-them back.  Needs the reference checkout (default /root/reference, or argv[1]); run
-once in the development container, output committed.  The GPU box never runs it.
+them back.  Needs the reference checkout (its directory as argv[1] or in
+NANOVLLM_REF); run once in the development container, output committed.  The GPU
+box never runs it.
 
 Usage:  python tests/golden/gen_sampler_golden.py [REF_DIR]
 """
@@ -17,7 +18,9 @@ os.environ.setdefault("TORCH_COMPILE_DISABLE", "1")
 import numpy as np
 import torch
 
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("NANOVLLM_REF", "")
+if not os.path.isdir(os.path.join(REF, "nanovllm")):
+    sys.exit(__doc__)
 sys.path.insert(0, REF)
 from nanovllm.layers.sampler import Sampler  # noqa: E402
 

@@ -2,9 +2,9 @@
 
 Runs nano-vLLM's Triton `store_kvcache` (nanovllm/layers/attention.py:10-40)
 on CPU tensors under TRITON_INTERPRET=1 and records inputs and the caches it
-produced.  Needs the reference checkout (default /root/reference, or the
-path given as argv[1]) and triton; it is run once in the development
-container, and its output is committed.  The GPU box never runs it.
+produced.  Needs the reference checkout (its directory as argv[1] or in
+NANOVLLM_REF) and triton; it is run once in the development container, and its
+output is committed.  The GPU box never runs it.
 
 Usage:  TRITON_INTERPRET=1 python tests/golden/gen_store_golden.py [REF_DIR]
 """
@@ -15,7 +15,9 @@ os.environ.setdefault("TRITON_INTERPRET", "1")
 import numpy as np
 import torch
 
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("NANOVLLM_REF", "")
+if not os.path.isdir(os.path.join(REF, "nanovllm")):
+    sys.exit(__doc__)
 sys.path.insert(0, REF)
 from nanovllm.layers.attention import store_kvcache  # noqa: E402
 
