@@ -70,3 +70,42 @@ def test_shards_partition_the_heads(world):
     qs = [shard_heads(case, r, world)[0] for r in range(world)]
     assert np.array_equal(np.concatenate(qs, axis=2), case.q)
     assert all(q.shape[2] == 32 // world for q in qs)
+
+
+def _dying_worker(rank, world, port, ret):
+    """Rank 1 leaves between steps (raises before its next collective); rank 0 must get an
+    error from that collective within the process group's short timeout, not wait forever."""
+    from datetime import timedelta
+    import time
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
+    t = torch.ones(4)
+    dist.all_reduce(t)  # step 1: both ranks
+    if rank == 1:
+        ret[1] = "left"
+        os._exit(0)      # gone before step 2, with no collective in flight
+    t0 = time.time()
+    try:
+        dist.all_reduce(t)  # step 2: the peer never joins
+        ret[0] = "completed"
+    except Exception as e:  # gloo reports the closed peer or the timeout
+        ret[0] = ("error", round(time.time() - t0, 1), type(e).__name__)
+
+
+def test_dead_rank_ends_the_next_collective_with_an_error():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    ret = ctx.Manager().dict()
+    procs = [ctx.Process(target=_dying_worker, args=(r, 2, port, ret)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert ret.get(1) == "left"
+    status = ret.get(0)
+    assert isinstance(status, tuple) and status[0] == "error" and status[1] < 30, status
