@@ -1,12 +1,14 @@
 /*
  * b200_attn.h — C ABI of the B200 (sm_100a) attention hot path of nano-vLLM.
  *
- * Every entry point takes plain device pointers, element strides and sizes,
- * enqueues its kernels on the caller's CUDA stream (a `cudaStream_t` passed
- * as `void*`), never synchronises the host, never allocates device memory
- * and never reads device data on the host.  That makes each call capturable
- * in a CUDA graph, which is how nano-vLLM runs decode
- * (nanovllm/engine/model_runner.py:222-257).
+ * Every entry point that launches work takes plain device pointers, element
+ * strides and sizes, enqueues its kernels on the caller's CUDA stream (a
+ * `cudaStream_t` passed as `void*`), never synchronises the host, never
+ * allocates device memory and never reads device data on the host.  That
+ * makes each call capturable in a CUDA graph, which is how nano-vLLM runs
+ * decode (nanovllm/engine/model_runner.py:222-257).  The diagnostic readers
+ * (b200_workspace_error, b200_varlen_prefill_error,
+ * b200_oproj_allreduce_error) synchronise the stream they are given.
  *
  * Return value: B200_OK or one of the error codes below.  The text of the
  * last error of the calling host thread is available from b200_last_error().
