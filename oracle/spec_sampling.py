@@ -11,6 +11,12 @@ al. 2023):
   if all k drafts are accepted: sample a bonus token from p_k,
 with p = softmax(target_logits / T) and q = softmax(draft_logits / T).
 
+Pinning: the reference has nothing to pin against.  The acceptance rule is pinned to an
+independent implementation of the same scheme, vLLM 0.22's rejection sampler
+(vllm/v1/sample/rejection_sampler.py, run on CPU with the same uniforms): decisions equal on
+the committed cases (tests/golden/spec_accept_vllm.npz).  vLLM draws the residual token with an
+exponential race rather than an inverse CDF, so that step is pinned in distribution only.
+
 Every floating-point operation is defined in a fixed order with float32
 rounding, so that the CUDA kernel reproduces the decisions and the sampled
 tokens bit for bit given identical uniforms:

@@ -87,3 +87,26 @@ def test_temperature_and_invalid_draft():
     toks, num = ss.spec_accept_ref(c.target_logits, c.draft_logits, c.draft_tokens, c.u_accept, c.u_sample,
                                    c.temperatures)
     assert num[1] == 1 and 0 <= toks[1, 0] < 300
+
+
+def test_acceptance_matches_vllm_rejection_sampler():
+    """Pinned to vLLM 0.22's rejection sampler (an independent implementation of the same
+    standard scheme) run on CPU with the same uniforms (tests/golden/spec_accept_vllm.npz,
+    generator beside it): every sequence's number of accepted drafts and accepted prefix."""
+    import os
+    g = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "spec_accept_vllm.npz"))
+    names = sorted({k.split(".")[0] for k in g.files})
+    assert len(names) == 2
+    lengths_seen = set()
+    for name in names:
+        tl, dl, T, dt, u, vt = (g[name + s] for s in (".target_logits", ".draft_logits", ".temperatures",
+                                                       ".draft_tokens", ".u_accept", ".vllm_tokens"))
+        B = tl.shape[0]
+        accepted_vllm = (vt >= 0).sum(axis=1) - 1  # accepted drafts, then one recovered/bonus token
+        tokens, num = ss.spec_accept_ref(tl, dl, dt, u, np.full(B, 0.5, np.float32), T)
+        assert np.array_equal(num - 1, accepted_vllm), name
+        for b in range(B):
+            n = accepted_vllm[b]
+            assert np.array_equal(tokens[b, :n], vt[b, :n]) and np.array_equal(vt[b, :n], dt[b, :n])
+            lengths_seen.add((name, int(n)))
+    assert len({n for name, n in lengths_seen if name.startswith("b32_k7")}) == 8  # 0..7 accepted all occur
