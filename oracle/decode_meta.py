@@ -7,6 +7,8 @@ Restates nanovllm/engine/model_runner.py:123-127 (prepare_block_tables), :167-18
   slot_mapping = block_table[-1] * block_size + last_block_num_tokens - 1 with
   last_block_num_tokens = len - (len(block_table) - 1) * block_size
   (nanovllm/engine/sequence.py); block_tables padded with -1 to the longest table.
+Pinned to the reference builders' own output on reference Sequence objects
+(tests/golden/decode_meta.npz).
 """
 import numpy as np
 

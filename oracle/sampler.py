@@ -10,6 +10,8 @@ positive constant.  This module restates
     (j // 4, row, offset_lo, offset_hi), key (seed_lo, seed_hi), word j % 4,
     U = ((bits >> 8) + 0.5) * 2^-24, E = -log(U);
   * the fused score argmax in float64 (for comparisons that allow near-ties).
+Pinned: Philox to the published known-answer vectors; the reference formula to the
+reference Sampler's own tokens on its own Exp(1) draw (tests/golden/sampler.npz).
 """
 import numpy as np
 
