@@ -27,3 +27,24 @@ def decode_metadata_ref(seqs, block_size):
         last_n = lens[b] - (len(t) - 1) * block_size
         slots[b] = t[-1] * block_size + last_n - 1
     return toks, lens - 1, slots, lens.astype(np.int32), bt, temps
+
+
+def expand_packed_ref(packed, batch, width, block_size):
+    """The device kernel's expansion (learn-nano-vllm_b200/csrc/decode_meta.cu) of the packed
+    int32 buffer [B lengths | B last tokens | B temperature bits | B + 1 block-list offsets |
+    block ids] into (input_ids, positions, slot_mapping, context_lens, block_tables [B, width],
+    temperatures)."""
+    h = np.asarray(packed, np.int32)
+    B = batch
+    lens, toks = h[:B], h[B:2 * B]
+    temps = h[2 * B:3 * B].view(np.float32)
+    offs, flat = h[3 * B:4 * B + 1], h[4 * B + 1:]
+    bt = np.full((B, width), -1, np.int32)
+    slots = np.full(B, -1, np.int32)
+    for b in range(B):
+        n = int(offs[b + 1] - offs[b])
+        bt[b, :n] = flat[offs[b]:offs[b + 1]]
+        if n > 0:
+            slots[b] = flat[offs[b] + n - 1] * block_size + (lens[b] - (n - 1) * block_size) - 1
+    return (toks.astype(np.int64), (lens - 1).astype(np.int64), slots, lens.astype(np.int32), bt,
+            temps.astype(np.float32))

@@ -69,3 +69,33 @@ def test_pack_worker_sequences(DecodeMetadata):
     B = len(SEQS)
     assert np.array_equal(np.delete(h, range(2 * B, 3 * B)), np.delete(full, range(2 * B, 3 * B)))
     assert np.all(h[2 * B:3 * B].view(np.float32) == 1.0)
+
+
+def test_pack_then_kernel_expansion_equals_reference_builders(DecodeMetadata):
+    """Random batches: DecodeMetadata.pack followed by the kernel's expansion (restated in
+    numpy) gives the reference builders' tensors (oracle pinned to them), on rank 0 and, apart
+    from temperatures, on worker ranks."""
+    from oracle.decode_meta import decode_metadata_ref, expand_packed_ref
+    rng = np.random.default_rng(5)
+    for trial in range(60):
+        B = int(rng.integers(1, 40))
+        ids = rng.permutation(4096)
+        seqs, used = [], 0
+        for _ in range(B):
+            n = int(rng.integers(1, 3000))
+            nb = (n + 255) // 256
+            seqs.append(FullSeq(n, int(rng.integers(0, 151936)), float(rng.uniform(0.1, 2.0)),
+                                [int(x) for x in ids[used:used + nb]]))
+            used += nb
+        size, W = DecodeMetadata.packed_size(seqs)
+        h = np.zeros(size, np.int32)
+        DecodeMetadata.pack(seqs, h)
+        got = expand_packed_ref(h, B, W, 256)
+        want = decode_metadata_ref([(len(s), s.last_token, s.temperature, s.block_table) for s in seqs], 256)
+        for g, w in zip(got, want):
+            assert g.dtype == w.dtype and np.array_equal(g, w)
+        hw = np.zeros(size, np.int32)
+        DecodeMetadata.pack([WorkerSeq(s) for s in seqs], hw, temperatures=False)
+        gw = expand_packed_ref(hw, B, W, 256)
+        for g, w in zip(gw[:5], want[:5]):
+            assert np.array_equal(g, w)
