@@ -1,7 +1,4 @@
 """Device decode metadata against the reference's own prepare_decode / prepare_sample."""
-import os
-import sys
-
 import numpy as np
 import pytest
 import torch
@@ -9,9 +6,6 @@ import torch
 from oracle.decode_meta import decode_metadata_ref
 
 pytestmark = pytest.mark.gpu
-
-ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-REF = os.path.join(ROOT, "baseline", "_ref")
 
 
 class _Seq:
@@ -63,10 +57,7 @@ def test_staging_reuse_across_steps(pkg):
             assert (got.cpu().numpy() == ref).all()
 
 
-def test_matches_reference_prepare_decode(pkg):
-    if not os.path.isdir(os.path.join(REF, "nanovllm")):
-        pytest.skip("reference not installed in baseline/_ref")
-    sys.path.insert(0, REF)
+def test_matches_reference_prepare_decode(pkg, nanovllm_ref):
     from nanovllm.engine.model_runner import ModelRunner
     from nanovllm.utils import context as ref_ctx
 

@@ -1,12 +1,10 @@
 """install() on the reference's own Qwen3Attention: the fused q/k epilogue against the
 module's stock forward (RMSNorm + RotaryEmbedding + store, then this package's Attention).
 
-Needs the unmodified reference installed in baseline/_ref (the bench's reference arm);
-skipped otherwise.
+Runs the unmodified reference from baseline/_ref (installed by __graft_entry__.build());
+fails when it is missing.
 """
-import os
 import socket
-import sys
 
 import numpy as np
 import pytest
@@ -14,15 +12,10 @@ import torch
 
 pytestmark = pytest.mark.gpu
 
-ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-REF = os.path.join(ROOT, "baseline", "_ref")
 
 
 @pytest.fixture(scope="module")
-def qwen3_attn(pkg):
-    if not os.path.isdir(os.path.join(REF, "nanovllm")):
-        pytest.skip("reference not installed in baseline/_ref")
-    sys.path.insert(0, REF)
+def qwen3_attn(pkg, nanovllm_ref):
     import torch.distributed as dist
     from nanovllm.models import qwen3
     from nanovllm.utils import context as ref_ctx

@@ -19,9 +19,6 @@ import torch.multiprocessing as mp
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 REF = os.path.join(ROOT, "baseline", "_ref")
 
-pytestmark = pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "nanovllm")),
-                                reason="reference not installed in baseline/_ref")
-
 
 class StandIn:
     """F.linear then all_reduce, recording each call's shapes."""
@@ -102,7 +99,7 @@ def _fp32_copy(layer, linear):
     return lay
 
 
-def test_row_parallel_dispatch_two_ranks():
+def test_row_parallel_dispatch_two_ranks(nanovllm_ref):
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
