@@ -7,8 +7,15 @@
  * allocates device memory and never reads device data on the host.  That
  * makes each call capturable in a CUDA graph, which is how nano-vLLM runs
  * decode (nanovllm/engine/model_runner.py:222-257).  The diagnostic readers
- * (b200_workspace_error, b200_varlen_prefill_error,
- * b200_oproj_allreduce_error) synchronise the stream they are given.
+ * (b200_workspace_error, b200_paged_attention_noalloc_error,
+ * b200_varlen_prefill_error, b200_oproj_allreduce_error) synchronise the
+ * stream they are given.
+ *
+ * Every wait inside a kernel is bounded (1 s).  One that runs out sets a bit
+ * of the call's device-side error word and the kernel returns; the results of
+ * that call are then undefined.  Bits: 1 a pipeline stage was never filled,
+ * 2 a stage was never released, 4 copies in flight did not complete before
+ * exit, 8 a barrier among the kernel's own warps ran out.
  *
  * Return value: B200_OK or one of the error codes below.  The text of the
  * last error of the calling host thread is available from b200_last_error().
@@ -237,9 +244,11 @@ B200_API int32_t b200_paged_attention(void* out, const void* q, int64_t q_stride
  * process exits.  Limit: batch * num_kv_heads <= 8192 and at most
  * (32 MiB - 33 KiB) / (query_len * Hq/Hkv * 516 B) work items; larger calls
  * return B200_ERR_WORKSPACE.  The first call on a device looks up the array's
- * device address (make it before any stream capture).  Calls share the array:
- * each clears the control words it needs, and calls that overlap on the GPU
- * race, so serialise them.
+ * device address (make it before any stream capture); the lookup is repeated
+ * in any other CUDA context of that device (a driver-API context, the new
+ * primary context after cudaDeviceReset).  Calls share the array: each clears
+ * the control words it needs (the error word included), and calls that
+ * overlap on the GPU race, so serialise them.
  */
 B200_API int32_t b200_paged_attention_noalloc(void* out, const void* q, int64_t q_stride_token,
                                      const void* k_cache, const void* v_cache,
@@ -256,6 +265,25 @@ B200_API int32_t b200_paged_attention_noalloc(void* out, const void* q, int64_t 
  * results of that call are undefined.  For tests and diagnostics only.
  */
 B200_API int32_t b200_workspace_error(const void* workspace, void* stream, int32_t* flag);
+
+/*
+ * Copies the device-side error word of the latest b200_paged_attention_noalloc
+ * call on the current device (it lives in the library's built-in scratch) to
+ * *flag, synchronously on `stream`; the bits are those listed at the top of
+ * this file.  No counterpart in the reference.  For tests and diagnostics.
+ */
+B200_API int32_t b200_paged_attention_noalloc_error(void* stream, int32_t* flag);
+
+/*
+ * Test hook, no counterpart in the reference: the next `launches`
+ * paged-attention launches (either entry point) made by the calling host
+ * thread run with an idle producer warp that issues no loads, and with every
+ * wait limited to wait_limit_ns (1 us .. 1 s).  The consumer warps' first wait
+ * then runs out, the call's error word gets bit 1 and the kernel returns (the
+ * output is undefined); nothing faults and later calls run normally.  Lets a
+ * test check that a wait that runs out is reported to the host.
+ */
+B200_API int32_t b200_testing_idle_producer(int32_t launches, int64_t wait_limit_ns);
 
 /*
  * Causal varlen prefill attention, optionally over the paged cache (prefix

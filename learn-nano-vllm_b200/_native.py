@@ -24,6 +24,8 @@ SIGNATURES = {
     "b200_paged_attention_noalloc": (_I32, [_P, _P, _I64, _P, _P, _I32, _I32, _P, _I32, _P, _I32, _I32, _I32,
                                             _I32, _I32, _F, _I32, _P]),
     "b200_workspace_error": (_I32, [_P, _P, ctypes.POINTER(ctypes.c_int32)]),
+    "b200_paged_attention_noalloc_error": (_I32, [_P, ctypes.POINTER(ctypes.c_int32)]),
+    "b200_testing_idle_producer": (_I32, [_I32, _I64]),
     "b200_varlen_prefill": (_I32, [_P, _P, _I64, _P, _I64, _P, _I64, _P, _P, _I32, _I32, _I32, _I32, _I32, _P,
                                    _I32, _I32, _I32, _I32, _I32, _F, _I32, _P]),
     "b200_varlen_prefill_error": (_I32, [_P, ctypes.POINTER(ctypes.c_int32)]),

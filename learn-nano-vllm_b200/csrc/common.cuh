@@ -39,7 +39,7 @@ int32_t make_tmap_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_
     } while (0)
 
 // Device-side error codes written to the workspace's error word.
-enum : int32_t { DEV_ERR_WAIT_FULL = 1, DEV_ERR_WAIT_EMPTY = 2, DEV_ERR_WAIT_DRAIN = 4 };
+enum : int32_t { DEV_ERR_WAIT_FULL = 1, DEV_ERR_WAIT_EMPTY = 2, DEV_ERR_WAIT_DRAIN = 4, DEV_ERR_WAIT_PEER = 8 };
 
 // Bounded spin-waits give up after this many nanoseconds (%globaltimer).
 constexpr uint64_t kWaitLimitNs = 1000ull * 1000ull * 1000ull;  // 1 s
@@ -96,13 +96,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Waits for completion of the barrier phase with the given parity; returns
-// false if that did not happen within kWaitLimitNs.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// false if that did not happen within limit_ns.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns = kWaitLimitNs) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     while (true) {
         if (mbar_try_wait(bar, parity)) return true;
-        if (global_timer_ns() - t0 > kWaitLimitNs) return false;
+        if (global_timer_ns() - t0 > limit_ns) return false;
     }
 }
 
@@ -121,12 +121,12 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
 
 // Polling wait for latency-critical single threads (a suspended try_wait can
 // resume up to ~1 us after the phase completes); same kWaitLimitNs bound.
-__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, uint64_t limit_ns = kWaitLimitNs) {
     if (mbar_test_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     for (uint32_t i = 1;; ++i) {
         if (mbar_test_wait(bar, parity)) return true;
-        if ((i & 63) == 0 && global_timer_ns() - t0 > kWaitLimitNs) return false;
+        if ((i & 63) == 0 && global_timer_ns() - t0 > limit_ns) return false;
     }
 }
 

@@ -31,6 +31,12 @@
 // sum, O) in registers with warp-shuffle row reductions; the eight partial
 // states are combined through shared memory at the end of an item (8 -> 4
 // in registers, then 4 -> 1).
+//
+// Every wait in the kernel is bounded (kWaitLimitNs, or the test limit): the
+// stage barriers, and the consumer warps' own barrier around the combine,
+// which is an mbarrier with one arrival per consumer thread rather than a
+// bar.sync, so that a warp whose sibling left the loop on an error gives up
+// after the limit instead of waiting for it forever.
 #include <climits>
 #include <mutex>
 
@@ -52,7 +58,6 @@ constexpr int kCtrlWords = 64;               // [0] next item, [1] finished CTAs
 constexpr size_t kFixedBytes = kCtrlWords * 4 + size_t(kCounterSlots) * 4;
 constexpr int kWaves = 4;
 constexpr int kChunkMaxTiles = 32;           // at most 4096 tokens per item
-constexpr int kSplitBarrier = 1;             // named barrier of the consumer warps
 constexpr int kRemBits = 12;                 // packed offsets: full-chunk offset << 12 | remainder offset
 
 struct Header {
@@ -69,6 +74,8 @@ struct Params {
     const int32_t* context_lens;
     int32_t batch, lq, hq, hkv, group, rows, block_size, num_blocks;
     float scale_log2;
+    uint64_t wait_ns;  // limit of every wait (kWaitLimitNs; shorter under the idle-producer test)
+    int32_t idle_producer;  // test hook: the producer issues nothing, so the consumers' first wait runs out
     int32_t* ctrl;
     int32_t* counters;
     float* part_o;    // [max_items][rows][kD]
@@ -86,6 +93,7 @@ struct Smem {
     Header hdr[NS];
     uint64_t full[NS];
     uint64_t empty[NS];
+    uint64_t cbar;                  // consumer barrier: kConsumers arrivals per phase
     int32_t off[kMaxBatch + 1];     // (full-chunk offset << kRemBits) | remainder offset
     int32_t red[kThreads / 32 + 1];
     int32_t flag;
@@ -124,6 +132,16 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* red, int* total)
     __syncthreads();
     *total = tot;
     return base + x - v;
+}
+
+// Barrier of the consumer threads, bounded: each arrives (release) and polls
+// the phase (acquire) for at most limit_ns.  Returns false, for the whole
+// warp alike, when the wait of any of its lanes ran out.
+__device__ __forceinline__ bool consumer_sync(uint64_t* bar, uint32_t& phase, uint64_t limit_ns) {
+    mbar_arrive(bar);
+    const bool ok = mbar_wait_spin(bar, phase, limit_ns);
+    phase ^= 1;
+    return __all_sync(0xffffffffu, ok);
 }
 
 // Chunk layout of one sequence: nt tiles cut into `full` chunks of `chunk`
@@ -203,6 +221,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&sm.full[s], 1);
             mbar_init(&sm.empty[s], kConsumerWarps);
         }
+        mbar_init(&sm.cbar, kConsumers);
         sm.err = 0;
         fence_mbar_init();
     }
@@ -265,7 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (warp == kConsumerWarps) {
         // ------------------------------------------------------------ producer
-        if (lane == 0) {
+        if (lane == 0 && !p.idle_producer) {
             const uint64_t pol = l2_policy_evict_first();
             const uint32_t q_bytes = uint32_t(p.group) * kD * 2;  // one query token's rows of this kv head
             int stage = 0;
@@ -286,7 +305,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 int next_claim = claim;
                 nxt.item = total_items;
                 for (int t = t0; t < t1; ++t) {
-                    if (!mbar_wait(&sm.empty[stage], phase ^ 1)) {
+                    if (!mbar_wait(&sm.empty[stage], phase ^ 1, p.wait_ns)) {
                         atomicOr(&p.ctrl[2], DEV_ERR_WAIT_EMPTY);
                         ok = false;
                         break;
@@ -339,7 +358,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 claim = next_claim;
             }
             if (ok) {
-                if (mbar_wait(&sm.empty[stage], phase ^ 1)) {
+                if (mbar_wait(&sm.empty[stage], phase ^ 1, p.wait_ns)) {
                     sm.hdr[stage].item = -1;  // sentinel: no more tiles
                     mbar_arrive(&sm.full[stage]);
                 } else {
@@ -353,7 +372,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int s = 0; s < NS; ++s) {
                     if (fills <= s) break;
                     const int64_t last = s + ((fills - 1 - s) / NS) * NS;
-                    if (!mbar_wait(&sm.full[s], uint32_t((last / NS) & 1))) atomicOr(&p.ctrl[2], DEV_ERR_WAIT_DRAIN);
+                    if (!mbar_wait(&sm.full[s], uint32_t((last / NS) & 1), p.wait_ns))
+                        atomicOr(&p.ctrl[2], DEV_ERR_WAIT_DRAIN);
                 }
             }
         }
@@ -367,20 +387,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int kadd = mi & 1, vadd = mi >> 1;
         const float sl2 = p.scale_log2;
         int stage = 0;
-        uint32_t phase = 0;
+        uint32_t phase = 0, cphase = 0;
         float m_run[2], l_run[2];
         float o[16][4];
         uint32_t qa[8][4];
         int lim[2];
         while (true) {
-            if (!mbar_wait(&sm.full[stage], phase)) {
+            // Exit decisions are warp-uniform (the lanes' waits can disagree at the limit).
+            if (!__all_sync(0xffffffffu, mbar_wait(&sm.full[stage], phase, p.wait_ns))) {
                 atomicOr(&p.ctrl[2], DEV_ERR_WAIT_FULL);
                 *reinterpret_cast<volatile int32_t*>(&sm.err) = 1;
                 break;
             }
-            // A sibling consumer warp that gave up will not reach the named
-            // barriers below: leave together instead of waiting for it.
-            if (*reinterpret_cast<volatile int32_t*>(&sm.err)) break;
+            // A sibling consumer warp that gave up will not reach the consumer
+            // barrier below: leave now rather than run into its time limit.
+            if (__any_sync(0xffffffffu, *reinterpret_cast<volatile int32_t*>(&sm.err) != 0)) break;
             const Header hd = sm.hdr[stage];
             if (hd.item < 0) break;
             if (hd.flags & kFirst) {
@@ -527,7 +548,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 make_float2(o[n][2 * hr], o[n][2 * hr + 1]);
                     }
                 }
-                named_bar_sync(kSplitBarrier, kConsumers);
+                if (!consumer_sync(&sm.cbar, cphase, p.wait_ns)) {
+                    atomicOr(&p.ctrl[2], DEV_ERR_WAIT_PEER);
+                    *reinterpret_cast<volatile int32_t*>(&sm.err) = 1;
+                    break;
+                }
                 if (warp < kHalf) {
 #pragma unroll
                     for (int hr = 0; hr < (ROWS_HI ? 2 : 1); ++hr) {
@@ -548,7 +573,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                     }
                 }
-                named_bar_sync(kSplitBarrier, kConsumers);
+                if (!consumer_sync(&sm.cbar, cphase, p.wait_ns)) {
+                    atomicOr(&p.ctrl[2], DEV_ERR_WAIT_PEER);
+                    *reinterpret_cast<volatile int32_t*>(&sm.err) = 1;
+                    break;
+                }
                 // 4 -> 1 over shared memory, one output element per thread and round.
                 const bool single = hd.nchunks == 1;
                 const int nel = p.rows * kD;
@@ -580,7 +609,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!single) {
                     // Publish this chunk (one release fence per CTA, cumulative over
                     // the barrier), then count it; the last chunk's CTA merges.
-                    named_bar_sync(kSplitBarrier, kConsumers);
+                    if (!consumer_sync(&sm.cbar, cphase, p.wait_ns)) {
+                        atomicOr(&p.ctrl[2], DEV_ERR_WAIT_PEER);
+                        *reinterpret_cast<volatile int32_t*>(&sm.err) = 1;
+                        break;
+                    }
                     if (tid == 0) {
                         __threadfence();
                         const int prev = atomicAdd(&p.counters[hd.b * p.hkv + hd.h], 1);
@@ -588,7 +621,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (last) __threadfence();
                         sm.flag = last;
                     }
-                    named_bar_sync(kSplitBarrier, kConsumers);
+                    if (!consumer_sync(&sm.cbar, cphase, p.wait_ns)) {
+                        atomicOr(&p.ctrl[2], DEV_ERR_WAIT_PEER);
+                        *reinterpret_cast<volatile int32_t*>(&sm.err) = 1;
+                        break;
+                    }
                     if (sm.flag) {
                         const int full = hd.nchunks - (seq_chunks(hd.ctx, cap, chunk).rem);
                         for (int idx = tid; idx < nel; idx += kConsumers) {
@@ -614,7 +651,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (tid == 0) p.counters[hd.b * p.hkv + hd.h] = 0;
                     }
                 }
-                named_bar_sync(kSplitBarrier, kConsumers);
+                if (!consumer_sync(&sm.cbar, cphase, p.wait_ns)) {
+                    atomicOr(&p.ctrl[2], DEV_ERR_WAIT_PEER);
+                    *reinterpret_cast<volatile int32_t*>(&sm.err) = 1;
+                    break;
+                }
             }
         }
     }
@@ -631,8 +672,34 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// Test hook state of the calling host thread (b200_testing_idle_producer).
+thread_local int g_idle_launches = 0;
+thread_local uint64_t g_idle_wait_ns = kWaitLimitNs;
+
+// Wait limit and idle-producer flag of the next launch on this host thread.
+inline void apply_test_hook(Params& prm) {
+    prm.wait_ns = kWaitLimitNs;
+    prm.idle_producer = 0;
+    if (g_idle_launches > 0) {
+        --g_idle_launches;
+        prm.wait_ns = g_idle_wait_ns;
+        prm.idle_producer = 1;
+    }
+}
+
 }  // namespace pa
 }  // namespace b200
+
+extern "C" int32_t b200_testing_idle_producer(int32_t launches, int64_t wait_limit_ns) {
+    using namespace b200;
+    clear_error();
+    B200_REQUIRE(launches >= 0, "testing_idle_producer: launches %d < 0", launches);
+    B200_REQUIRE(wait_limit_ns >= 1000 && wait_limit_ns <= int64_t(kWaitLimitNs),
+                 "testing_idle_producer: wait limit %lld ns outside [1 us, 1 s]", (long long)wait_limit_ns);
+    pa::g_idle_launches = launches;
+    pa::g_idle_wait_ns = uint64_t(wait_limit_ns);
+    return B200_OK;
+}
 
 extern "C" size_t b200_paged_attention_workspace_size(int32_t max_items, int32_t query_len, int32_t group_size,
                                                       int32_t head_dim) {
@@ -721,6 +788,7 @@ extern "C" int32_t b200_paged_attention(void* out, const void* q, int64_t q_stri
     prm.part_o = reinterpret_cast<float*>(ws + kFixedBytes);
     prm.part_lse = prm.part_o + max_items * rows * kD;
     prm.max_items = int32_t(max_items > INT32_MAX / 2 ? INT32_MAX / 2 : max_items);
+    apply_test_hook(prm);
 
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const dim3 grid(device_sm_count()), block(kThreads);
@@ -758,11 +826,16 @@ extern "C" int32_t b200_paged_attention(void* out, const void* q, int64_t q_stri
 // that array until the process exits.  The array's host-side name is only a
 // stand-in for the symbol, so the first call on each device looks up its
 // device address with cudaGetSymbolAddress (with that device current) and
-// caches it; make that first call before any stream capture.  All calls
+// caches it; make that first call before any stream capture.  The cache is
+// keyed by the current CUDA context's unique id (cuCtxGetId), so a call made
+// in another context on the same device (a driver-API context, or the new
+// primary context after cudaDeviceReset) looks the address up again instead
+// of reusing one that belongs to a destroyed or different context.  All calls
 // share the one array and it keeps the last call's contents: each call
-// clears the control words and split counters it uses before launching,
-// and calls that overlap on the GPU (two streams, two host threads) race
-// on it and must be serialised by the caller.
+// clears the control words (error word included) and split counters it uses
+// before launching, and calls that overlap on the GPU (two streams, two host
+// threads) race on it and must be serialised by the caller.
+// b200_paged_attention_noalloc_error reads the error word of the latest call.
 namespace b200 {
 namespace pa {
 
@@ -775,24 +848,62 @@ static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes]
 namespace {
 constexpr int kNoAllocMaxDevices = 64;
 std::mutex g_noalloc_mu;
-void* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+struct ScratchAddr {
+    unsigned long long ctx_id;  // unique id of the context the address belongs to (0: none yet)
+    void* ptr;
+};
+ScratchAddr g_noalloc_addr[kNoAllocMaxDevices] = {};
 
-// Device address of g_noalloc_scratch on the current device (looked up once per device).
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+CtxGetCurrentFn g_ctx_current = nullptr;
+CtxGetIdFn g_ctx_id = nullptr;
+std::once_flag g_ctx_fns_once;
+
+// Unique id of the calling thread's current CUDA context, 0 if there is none
+// or the driver does not report it (then nothing is cached).
+unsigned long long current_ctx_id() {
+    std::call_once(g_ctx_fns_once, [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_ctx_current = reinterpret_cast<CtxGetCurrentFn>(fn);
+        fn = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_ctx_id = reinterpret_cast<CtxGetIdFn>(fn);
+    });
+    if (!g_ctx_current || !g_ctx_id) return 0;
+    CUcontext ctx = nullptr;
+    unsigned long long id = 0;
+    if (g_ctx_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return 0;
+    if (g_ctx_id(ctx, &id) != CUDA_SUCCESS) return 0;
+    return id;
+}
+
+// Device address of g_noalloc_scratch in the current context of the current
+// device: looked up once per (device, context) and cached.
 int32_t noalloc_scratch(void** out) {
     int dev = 0;
     B200_CUDA_TRY(cudaGetDevice(&dev));
     if (dev < 0 || dev >= kNoAllocMaxDevices)
         return fail(B200_ERR_UNSUPPORTED, "paged_attention_noalloc: device %d beyond %d", dev, kNoAllocMaxDevices);
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    if (g_noalloc_ptr[dev] == nullptr) {
-        void* p = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-        if (e != cudaSuccess || p == nullptr)
-            return fail(B200_ERR_CUDA, "paged_attention_noalloc: cudaGetSymbolAddress failed: %s",
-                        cudaGetErrorString(e));
-        g_noalloc_ptr[dev] = p;
+    const unsigned long long id = current_ctx_id();
+    if (id != 0 && g_noalloc_addr[dev].ctx_id == id) {
+        *out = g_noalloc_addr[dev].ptr;
+        return B200_OK;
     }
-    *out = g_noalloc_ptr[dev];
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr)
+        return fail(B200_ERR_CUDA, "paged_attention_noalloc: cudaGetSymbolAddress failed: %s",
+                    cudaGetErrorString(e));
+    // The lookup makes the runtime's context current if none was: key the cache on it.
+    g_noalloc_addr[dev].ctx_id = current_ctx_id();
+    g_noalloc_addr[dev].ptr = p;
+    *out = p;
     return B200_OK;
 }
 }  // namespace
@@ -884,6 +995,7 @@ extern "C" int32_t b200_paged_attention_noalloc(void* out, const void* q, int64_
     prm.part_o = reinterpret_cast<float*>(ws + kNoAllocFixedBytes);
     prm.part_lse = prm.part_o + max_items * rows * kD;
     prm.max_items = int32_t(max_items);
+    apply_test_hook(prm);
 
     const dim3 grid(device_sm_count()), block(kThreads);
     const bool hi = rows > 8;
@@ -902,5 +1014,18 @@ extern "C" int32_t b200_paged_attention_noalloc(void* out, const void* q, int64_
         else paged_attention_kernel<false, false><<<grid, block, smem, s>>>(prm, tmk, tmv);
     }
     B200_CUDA_TRY(cudaGetLastError());
+    return B200_OK;
+}
+
+extern "C" int32_t b200_paged_attention_noalloc_error(void* stream, int32_t* flag) {
+    using namespace b200;
+    using namespace b200::pa;
+    clear_error();
+    B200_REQUIRE(flag != nullptr, "paged_attention_noalloc_error: null pointer");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // The error word is the third int32 of the control block at the start of the scratch.
+    B200_CUDA_TRY(cudaMemcpyFromSymbolAsync(flag, g_noalloc_scratch, sizeof(int32_t), 2 * sizeof(int32_t),
+                                            cudaMemcpyDeviceToHost, s));
+    B200_CUDA_TRY(cudaStreamSynchronize(s));
     return B200_OK;
 }

@@ -186,3 +186,22 @@ def test_against_flash_attn_golden(pkg, name):
     out = pkg.paged_attention(dev_bf16(q), dev_bf16(k), dev_bf16(v), dev_i32(c.context_lens),
                               dev_i32(c.block_tables), c.scale)
     assert_attn_close(host(out), want.reshape(q.shape), name)
+
+
+def test_wait_that_runs_out_is_reported(pkg):
+    """A stage that is never filled: with the test hook the producer warp issues no loads and
+    every wait is limited to 2 ms.  The call must return with error bit 1 in its workspace
+    (no hang, no fault), and the next call on the same workspace must run normally."""
+    lib = pkg.lib()
+    case = cases.make_paged_case([300, 1100, 5, 2600], 16, 8, lq=1, seed=3)
+    q, kc, vc = dev_bf16(case.q), dev_bf16(case.k_cache), dev_bf16(case.v_cache)
+    cl, bt = dev_i32(case.context_lens), dev_i32(case.block_tables)
+    ws = torch.zeros(lib.b200_paged_attention_workspace_size(4096, 1, 2, 128), dtype=torch.uint8, device="cuda")
+    assert lib.b200_testing_idle_producer(1, 2_000_000) == 0
+    pkg.paged_attention(q, kc, vc, cl, bt, case.scale, workspace=ws)
+    assert pkg.workspace_error(ws) & 1
+    ws.zero_()  # the error word is sticky; the rest of the control region is re-armed by the kernel
+    out = pkg.paged_attention(q, kc, vc, cl, bt, case.scale, workspace=ws)
+    assert pkg.workspace_error(ws) == 0
+    want = oatt.paged_attention_ref(host(q), host(kc), host(vc), case.block_tables, case.context_lens, case.scale)
+    assert_attn_close(host(out), want, "after the stalled call")
