@@ -22,9 +22,10 @@ rounding, so that the CUDA kernel reproduces the decisions and the sampled
 tokens bit for bit given identical uniforms:
   * exp_c (for x <= 0): y = min(x*log2(e), 0); n = rint(y) by the magic
     constant 1.5*2^23 (t = y + c, n = t - c, round to nearest even);
-    f = y - n; P(f) = a degree-5 polynomial for 2^f on [-1/2, 1/2] (fitted
-    for relative error, 1.7e-7 at most, P(0) = 1; float32 coefficients
-    EXP2_COEF) by Horner with fused multiply-add (one rounding per step);
+    f = y - n; P(f) = a degree-5 polynomial for 2^f on [-1/2, 1/2] (the
+    minimax fit of the relative error with P(0) = 1, by linear programming,
+    1.6e-7 at most in float32; coefficients EXP2_COEF) by Horner with fused
+    multiply-add (one rounding per step);
     exp_c = P * 2^n (exponent field add), 0 below y = -125;
   * probabilities: p_j = exp_c(x_j - M) * r with r = 1 / S rounded once;
   * sums: the vocabulary is cut into tiles of 4096; in a tile, "thread" i
@@ -48,9 +49,11 @@ f32 = np.float32
 TILE = 4096
 THREADS = 256
 LOG2E = f32(1.4426950408889634)
-# 2^f ~ sum_k c_k f^k on [-1/2, 1/2]: relative-error fit with c_0 = 1 (float32)
-EXP2_COEF = [f32(float.fromhex(h)) for h in ("0x1.0p+0", "0x1.62e42ap-1", "0x1.ebf9bcp-3", "0x1.c6b752p-5",
-                                               "0x1.3cea88p-7", "0x1.5bba14p-10")]
+# 2^f ~ sum_k c_k f^k on [-1/2, 1/2] with c_0 = 1: discrete minimax of the relative error by
+# linear programming, rounded to float32 (learn-nano-vllm_b200/csrc/gen_exp2_coef.py; the CUDA
+# kernel holds the same literals, tests/test_oracle_spec.py checks all three agree)
+EXP2_COEF = [f32(float.fromhex(h)) for h in ("0x1.0p+0", "0x1.62e42ap-1", "0x1.ebf9aep-3", "0x1.c6b64ep-5",
+                                               "0x1.3cee66p-7", "0x1.5c10d4p-10")]
 
 
 def fma32(a, b, c):

@@ -110,3 +110,24 @@ def test_acceptance_matches_vllm_rejection_sampler():
             assert np.array_equal(tokens[b, :n], vt[b, :n]) and np.array_equal(vt[b, :n], dt[b, :n])
             lengths_seen.add((name, int(n)))
     assert len({n for name, n in lengths_seen if name.startswith("b32_k7")}) == 8  # 0..7 accepted all occur
+
+
+def test_exp2_coefficients_come_from_their_generator():
+    """exp_c's polynomial: the oracle's coefficients and the CUDA kernel's literals are
+    exactly what learn-nano-vllm_b200/csrc/gen_exp2_coef.py produces (minimax fit of the
+    relative error by linear programming, rounded to float32)."""
+    import importlib.util
+    import os
+    import re
+    csrc = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "learn-nano-vllm_b200", "csrc")
+    spec = importlib.util.spec_from_file_location("gen_exp2_coef", os.path.join(csrc, "gen_exp2_coef.py"))
+    gen = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(gen)
+    want = gen.coefficients_f32()
+    assert [float(c) for c in ss.EXP2_COEF] == [float(c) for c in want]
+    src = open(os.path.join(csrc, "spec_accept.cu")).read()
+    body = re.search(r"kExpCoef\[kExpDeg \+ 1\]\s*=\s*\{([^}]*)\}", src).group(1)
+    lits = [float.fromhex(t.strip().rstrip("f")) for t in body.split(",")]
+    assert lits == [float(c) for c in want]
+    _, t = gen.fit()
+    assert t < 1e-7
