@@ -42,3 +42,28 @@ def test_uncorrelated_drafts_mostly_rejected(pkg):
     toks, num, wt, wn = run(pkg, c)
     assert np.array_equal(num, wn) and np.array_equal(toks, wt)
     assert num.mean() < 2
+
+
+@pytest.mark.parametrize("name", ["independent", "correlated"])
+def test_config4_full_size_bit_exact(pkg, name):
+    """The speculative-verify configuration at full size (B = 128, k = 4, V = 151,936, logits
+    N(0, 2^2), seeded uniforms): every count and token equal to the oracle's, recorded in
+    tests/golden/spec_config4.npz by its generator (the inputs are regenerated from the seed and
+    checked against the recorded checksum), and to the live oracle on 16 sampled sequences."""
+    import os
+    import sys
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden"))
+    import gen_spec_config4_golden as gen
+    fx = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "spec_config4.npz"))
+    c = cases.make_spec_case(gen.B, gen.K, gen.V, **gen.CASES[name])
+    assert np.array_equal(gen.input_checksum(c), fx[f"{name}_checksum"]), "regenerated inputs differ"
+    t = lambda x: torch.from_numpy(np.ascontiguousarray(x)).cuda()
+    toks, num = pkg.spec_accept(t(c.target_logits), t(c.draft_logits), t(c.draft_tokens), t(c.u_accept),
+                                t(c.u_sample), None)
+    toks, num = toks.cpu().numpy(), num.cpu().numpy()
+    assert np.array_equal(num, fx[f"{name}_num"])
+    assert np.array_equal(toks, fx[f"{name}_tokens"])
+    rows = np.random.default_rng(7).choice(gen.B, 16, replace=False)
+    wt, wn = ss.spec_accept_ref(c.target_logits[rows], c.draft_logits[rows], c.draft_tokens[rows], c.u_accept[rows],
+                                c.u_sample[rows], None)
+    assert np.array_equal(num[rows], wn) and np.array_equal(toks[rows], wt)
