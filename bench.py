@@ -10,16 +10,26 @@ their query heads (nanovllm/models/qwen3.py:29-35), so the total work is
 fixed (strong scaling) and ranks exchange nothing on the data path.
 
 A step is one decode step of that layer: the KV-cache scatter of the 512
-new tokens followed by paged decode attention over every cached token.  The
-per-rank cache (4.8 GB / N) is far larger than the 126 MB L2, so no flush is
-needed between steps.  Inputs are synthetic (random bf16, seeded).
+new tokens followed by paged decode attention over every cached token, and
+with N > 1 GPUs the row-parallel all-reduce of the layer's o_proj output
+([512, 4096] bf16, nanovllm/layers/linear.py:152-156) -- NCCL by default,
+or (--row-parallel fused) the o_proj GEMM and the all-reduce in one kernel
+of this package.  The per-rank cache (4.8 GB / N) is far larger than the
+126 MB L2, so no flush is needed between steps.  Inputs are synthetic
+(random bf16, seeded).
 
-  value      algorithmic HBM bytes of the step / device time (GB/s, all ranks)
+  value      algorithmic HBM bytes of scatter + attention / device time of
+             the whole step (GB/s, all ranks)
   e2e        the same bytes over the time of the user-facing call
-             (Attention.forward) with host-side inputs copied in and the
-             output copied back inside the timed region
+             (Attention.forward, plus the all-reduce at N > 1) with
+             host-side inputs copied in and the output copied back inside
+             the timed region; device-timed, with the wall-clock time beside
   roofline   the paged-attention kernel alone: bytes / CUDA-event duration,
              against MEASURED_PEAKS.json's HBM copy bandwidth
+  attention_us / row_parallel_us  each part of the step timed alone per rank
+             (max over ranks)
+  prefill_config3 / verify_config4  (1 GPU) the prefix-cached prefill and
+             the speculative verify configurations, kernels timed alone
   cpu_baseline  the numpy oracle of the same math on the host cores
 
 --impl reference times the reference path's math on the host CPU (the
@@ -29,7 +39,6 @@ import argparse
 import json
 import math
 import os
-import re
 import statistics
 import subprocess
 import sys
@@ -43,6 +52,13 @@ sys.path.insert(0, ROOT)
 HQ_TOTAL, HKV_TOTAL, HEAD_DIM, BLOCK = 32, 8, 128, 256
 BATCH, SIGMA, CAP = 512, 0.5, 32768
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+# DRAM bytes (read + write) per paged-attention launch over its algorithmic bytes, from one
+# ncu capture of a B = 64 case of the same context draw (ncu --set full --clock-control none
+# -k regex:paged_attention -s 2 -c 1 python bench.py --batch 64 --steps 3 --warmup 1
+# --no-cpu-baseline --no-extras); the full launch is too large to capture with every metric,
+# and its traffic grows in proportion (K/V rows are read once), so traffic is reported scaled.
+DRAM_TRAFFIC_RATIO = 1.034
 
 
 def parse():
@@ -67,6 +83,12 @@ def parse():
                          "(per-rank kernel efficiency at TP N without N GPUs)")
     ap.add_argument("--batch", type=int, default=BATCH,
                     help="sequences in the batch (profiling runs use a smaller batch; the bench line uses 512)")
+    ap.add_argument("--row-parallel", choices=["nccl", "fused", "none"], default="nccl",
+                    help="decode at N > 1: the row-parallel step inside the timed region -- nccl: dist.all_reduce "
+                         "of the o_proj output [B, 4096] bf16; fused: o_proj GEMM + all-reduce in one kernel of "
+                         "this package (OprojAllReduce); none: attention only")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="decode: leave out the prefill (config 3) and verify (config 4) keys")
     return ap.parse_args()
 
 
@@ -96,16 +118,13 @@ def measured_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def profiled_traffic(bytes_per_launch):
-    """DRAM bytes per paged-attention launch: the DRAM-traffic / algorithmic-bytes
-    ratio from the committed ncu summary times this launch's algorithmic bytes
-    (or None without a summary)."""
-    p = os.path.join(ROOT, "profiles", "paged_attention_config5.md")
+def _peak_tflops():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
-        m = re.search(r"dram_traffic_ratio:\s*([0-9.eE+]+)", open(p).read())
-        return round(float(m.group(1)) * bytes_per_launch) if m else None
-    except OSError:
-        return None
+        with open(p) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured (burst)"
+    except Exception:
+        return FALLBACK_BF16_TFLOPS, "fallback"
 
 
 def _all_host_threads():
@@ -289,10 +308,11 @@ def _time(torch, stream, fn, steps, warmup):
     return e0.elapsed_time(e1) / steps
 
 
-def run_prefill(args, pkg, torch, dev):
+def measure_prefill(pkg, torch, dev, steps, warmup):
     """Config 3: 64 sequences share a 768-token prefix (3 cached blocks), unique
     suffixes U[64, 512]; Qwen3-0.6B attention shape (16 q / 8 kv heads); scatter
-    of the suffix K/V + causal prefill over the paged cache."""
+    of the suffix K/V + causal prefill over the paged cache.  Returns the step
+    time, the prefill kernel alone (CUDA events) and its roofline."""
     hq, hkv, d, bs, prefix = 16, 8, 128, 256, 768
     rng = np.random.default_rng(0)
     suffix = rng.integers(64, 513, size=64).astype(np.int32)
@@ -330,28 +350,35 @@ def run_prefill(args, pkg, torch, dev):
     stream = torch.cuda.current_stream(dev)
     flops = 4.0 * hq * d * float((suffix.astype(np.float64) * prefix + suffix * (suffix + 1) / 2.0).sum())
     with ClockSampler(dev.index or 0) as clk:
-        ms = _time(torch, stream, step, args.steps, args.warmup)
-        kms = _time(torch, stream, attn, args.steps, args.warmup)
+        ms = _time(torch, stream, step, steps, warmup)
+        kms = _time(torch, stream, attn, steps, warmup)
     assert pkg.ops.prefill_error() == 0
     peak = _peak_tflops()
+    return {"workload": "config3: 64 seqs, shared 768-token prefix, suffix U[64,512], 16/8 heads, D 128",
+            "tokens": T, "ms_per_step": round(ms, 4), "step_TFLOPs": round(flops / (ms / 1e3) / 1e12, 2),
+            "roofline": {"bound": "tensor", "kernel": "prefill_kernel", "achieved": round(flops / (kms / 1e3) / 1e12, 1),
+                         "peak": peak[0], "peak_kind": peak[1], "unit": "TFLOP/s",
+                         "frac": round(flops / (kms / 1e3) / 1e12 / peak[0], 4), "us_per_launch": round(kms * 1e3, 2),
+                         "flops_per_launch": flops},
+            "clocks": clk.summary()}
+
+
+def run_prefill(args, pkg, torch, dev):
+    r = measure_prefill(pkg, torch, dev, args.steps, args.warmup)
     print(json.dumps({
-        "metric": "prefix-cached prefill attn TFLOP/s (useful causal flops)", "value": round(flops / (ms / 1e3) / 1e12, 2),
-        "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "metric": "prefix-cached prefill attn TFLOP/s (useful causal flops)", "value": r["step_TFLOPs"],
+        "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_per_step"],
         "higher_is_better": True, "dtype": "bf16", "data": "synthetic (seeded random bf16)",
-        "config": {"workload": "config3: 64 seqs, shared 768-token prefix, suffix U[64,512], 16/8 heads, D 128",
-                   "tokens": T},
-        "roofline": {"bound": "tensor", "kernel": "prefill_kernel", "achieved": round(flops / (kms / 1e3) / 1e12, 1),
-                     "peak": peak[0], "peak_kind": peak[1], "unit": "TFLOP/s",
-                     "frac": round(flops / (kms / 1e3) / 1e12 / peak[0], 4), "us_per_launch": round(kms * 1e3, 2),
-                     "flops_per_launch": flops},
-        "clocks": clk.summary()}), flush=True)
+        "config": {"workload": r["workload"], "tokens": r["tokens"]},
+        "roofline": r["roofline"], "clocks": r["clocks"]}), flush=True)
 
 
-def run_verify(args, pkg, torch, dev):
+def measure_verify(pkg, torch, dev, steps, warmup):
     """Config 4: speculative verify on the Qwen3-0.6B attention shape -- B=128,
     k=4 drafts (5 queries each), context U[512, 4096]; scatter of the 5 new
     tokens, (k+1)-query paged attention, then acceptance sampling over
-    vocab 151936 (logits N(0, 2^2), drafts correlated with the target)."""
+    vocab 151936 (logits N(0, 2^2), drafts correlated with the target).
+    Returns the step time and each kernel timed alone (CUDA events)."""
     B, k, V, hq, hkv, d, bs = 128, 4, 151936, 16, 8, 128, 256
     rng = np.random.default_rng(0)
     ctx = rng.integers(512, 4097, size=B).astype(np.int32)
@@ -395,23 +422,34 @@ def run_verify(args, pkg, torch, dev):
     attn_bytes = int(ctx.sum()) * 2 * hkv * d * 2 + B * (k + 1) * hq * d * 2 * 2
     acc_bytes = (2 * k + 1) * B * V * 4
     with ClockSampler(dev.index or 0) as clk:
-        ms = _time(torch, stream, step, args.steps, args.warmup)
-        ams = _time(torch, stream, attn, args.steps, args.warmup)
-        sms = _time(torch, stream, accept, args.steps, args.warmup)
+        ms = _time(torch, stream, step, steps, warmup)
+        ams = _time(torch, stream, attn, steps, warmup)
+        sms = _time(torch, stream, accept, steps, warmup)
+    assert pkg.workspace_error(ws) == 0, "device wait timed out"
     flops = 4.0 * float(ctx.sum()) * (k + 1) * hq * d
     hbm = measured_peak()
+    tfl = _peak_tflops()
     toks, num = pkg.spec_accept(tl, dl, dt, ua, us, workspace=sws)
+    return {"workload": "config4: B=128, k=4, ctx U[512,4096], 16/8 heads, V 151936", "ms_per_step": round(ms, 4),
+            "attention": {"us": round(ams * 1e3, 2), "GBps": round(attn_bytes / (ams / 1e3) / 1e9, 1),
+                          "frac_hbm": round(attn_bytes / (ams / 1e3) / 1e9 / hbm[0], 4),
+                          "TFLOPs": round(flops / (ams / 1e3) / 1e12, 2),
+                          "frac_bf16_peak": round(flops / (ams / 1e3) / 1e12 / tfl[0], 4),
+                          "bytes_per_launch": attn_bytes, "flops_per_launch": flops},
+            "acceptance": {"us": round(sms * 1e3, 2), "GBps": round(acc_bytes / (sms / 1e3) / 1e9, 1),
+                           "frac_hbm": round(acc_bytes / (sms / 1e3) / 1e9 / hbm[0], 4),
+                           "mean_accepted": round(float(num.float().mean().item()) - 1, 3)},
+            "peaks": {"hbm_GBps": hbm[0], "hbm_kind": hbm[1], "bf16_TFLOPs": tfl[0], "bf16_kind": tfl[1]},
+            "clocks": clk.summary()}
+
+
+def run_verify(args, pkg, torch, dev):
+    r = measure_verify(pkg, torch, dev, args.steps, args.warmup)
     print(json.dumps({
-        "metric": "speculative verify step ms (attention + acceptance)", "value": round(ms, 4), "unit": "ms",
+        "metric": "speculative verify step ms (attention + acceptance)", "value": r["ms_per_step"], "unit": "ms",
         "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": False, "dtype": "bf16/fp32",
-        "data": "synthetic (seeded)", "config": {"workload": "config4: B=128, k=4, ctx U[512,4096], 16/8 heads, V 151936"},
-        "attention": {"us": round(ams * 1e3, 2), "GBps": round(attn_bytes / (ams / 1e3) / 1e9, 1),
-                      "frac_hbm": round(attn_bytes / (ams / 1e3) / 1e9 / hbm[0], 4),
-                      "TFLOPs": round(flops / (ams / 1e3) / 1e12, 2)},
-        "acceptance": {"us": round(sms * 1e3, 2), "GBps": round(acc_bytes / (sms / 1e3) / 1e9, 1),
-                       "frac_hbm": round(acc_bytes / (sms / 1e3) / 1e9 / hbm[0], 4),
-                       "mean_accepted": round(float(num.float().mean().item()) - 1, 3)},
-        "clocks": clk.summary()}), flush=True)
+        "data": "synthetic (seeded)", "config": {"workload": r["workload"]},
+        "attention": r["attention"], "acceptance": r["acceptance"], "clocks": r["clocks"]}), flush=True)
 
 
 def _time_graph(torch, stream, fn, steps, warmup, calls=20):
@@ -769,15 +807,6 @@ def run_engine(args, pkg):
         "clocks": clk.summary()}), flush=True)
 
 
-def _peak_tflops():
-    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
-    try:
-        with open(p) as f:
-            return float(json.load(f)["bf16_tflops"]), "measured (burst)"
-    except Exception:
-        return 1590.0, "fallback"
-
-
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -842,9 +871,29 @@ def main():
     scale = HEAD_DIM ** -0.5
     ws = pkg.paged_workspace(dev, 1, hq // hkv, BATCH * hkv)
 
+    # The row-parallel step that follows attention at N > 1 (linear.py:152-156): the o_proj
+    # output y [B, 4096] is all-reduced (NCCL), or o_proj and the all-reduce run as one kernel.
+    rp = args.row_parallel if world > 1 else "none"
+    hidden = HQ_TOTAL * HEAD_DIM
+    y = torch.randn(BATCH, hidden, generator=g, device=dev).to(torch.bfloat16) if rp != "none" else None
+    oproj, wo = None, None
+    if rp == "fused":
+        oproj = pkg.OprojAllReduce(dist.group.WORLD, max_tokens=BATCH, hidden=hidden)
+        wo = (torch.randn(hidden, hq * HEAD_DIM, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+
+    def row_parallel():
+        if rp == "nccl":
+            dist.all_reduce(y)
+        elif rp == "fused":
+            oproj(out.view(BATCH, hq * HEAD_DIM), wo, out=y)
+
+    def attention():
+        pkg.paged_attention(q.unsqueeze(1), kc, vc, cl, bt, scale, out=out, workspace=ws)
+
     def step():
         pkg.store_kvcache(kn, vn, kc, vc, slots)
-        pkg.paged_attention(q.unsqueeze(1), kc, vc, cl, bt, scale, out=out, workspace=ws)
+        attention()
+        row_parallel()
 
     def barrier():
         if world > 1:
@@ -866,17 +915,25 @@ def main():
         torch.cuda.synchronize(dev)
         barrier()
     ms = e0.elapsed_time(e1)
-    # -- the dominant kernel alone (paged attention), CUDA events on its stream
-    nk = max(20, min(args.steps, 200))
-    k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize(dev)
-    k0.record(stream)
-    for _ in range(nk):
-        pkg.paged_attention(q.unsqueeze(1), kc, vc, cl, bt, scale, out=out, workspace=ws)
-    k1.record(stream)
-    torch.cuda.synchronize(dev)
-    kern_ms = k0.elapsed_time(k1) / nk
+
+    def alone(fn, n):
+        """Per-call device time of fn alone, CUDA events on its stream."""
+        torch.cuda.synchronize(dev)
+        barrier()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record(stream)
+        for _ in range(n):
+            fn()
+        a1.record(stream)
+        torch.cuda.synchronize(dev)
+        return a0.elapsed_time(a1) / n
+
+    # -- each part of the step alone: the dominant kernel (paged attention), the row-parallel step
+    kern_ms = alone(attention, max(20, min(args.steps, 200)))
+    rp_ms = alone(row_parallel, max(20, min(args.steps, 200))) if rp != "none" else 0.0
     assert pkg.workspace_error(ws) == 0, "device wait timed out"
+    if oproj is not None:
+        assert oproj.error() == 0, "o_proj all-reduce wait timed out"
 
     # -- e2e: the user-facing Attention.forward with host inputs and output read-back
     from learn_nano_vllm_b200 import context as pctx
@@ -896,6 +953,10 @@ def main():
             d.copy_(h, non_blocking=True)
         pctx.set_context(False, slot_mapping=d_sl, context_lens=d_cl, block_tables=d_bt)
         o = attn(d_q, d_k, d_v)
+        if rp == "nccl":
+            dist.all_reduce(y)
+        elif rp == "fused":
+            oproj(o.view(BATCH, hq * HEAD_DIM), wo, out=y)
         h_out.copy_(o, non_blocking=True)
 
     for _ in range(3):
@@ -904,59 +965,78 @@ def main():
     torch.cuda.synchronize(dev)
     barrier()
     x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    w0 = time.perf_counter()
     x0.record(stream)
     for _ in range(ne):
         e2e_step()
     x1.record(stream)
     torch.cuda.synchronize(dev)
+    wall_ms = (time.perf_counter() - w0) * 1e3 / ne
     barrier()
     e2e_ms = x0.elapsed_time(x1) / ne
     pctx.reset_context()
 
+    # every rank on its own GPU, every rank in the communicator
+    gpus_active, comm_ok = 1, True
+    if world > 1:
+        uuids = [None] * world
+        dist.all_gather_object(uuids, str(torch.cuda.get_device_properties(dev).uuid))
+        gpus_active = len(set(uuids))
+        one = torch.ones(1, device=dev)
+        dist.all_reduce(one)
+        comm_ok = int(one.item()) == world == dist.get_world_size()
+
     dec_b, store_b = step_bytes(ctx, hq, hkv, width)
-    t = torch.tensor([ms, kern_ms, e2e_ms], dtype=torch.float64, device=dev)
+    t = torch.tensor([ms, kern_ms, e2e_ms, rp_ms, wall_ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, kern_ms, e2e_ms = t.tolist()
+    ms, kern_ms, e2e_ms, rp_ms, wall_ms = t.tolist()
+    if oproj is not None:
+        torch.cuda.synchronize(dev)
+        barrier()
+        del oproj
     total_bytes = (dec_b + store_b) * world
     value = total_bytes * args.steps / (ms / 1e3) / 1e9
     peak, peak_kind = measured_peak()
     achieved = dec_b / (kern_ms / 1e3) / 1e9
 
-    allreduce = None
-    if world > 1:  # the row-parallel all-reduce that follows o_proj (linear.py:155): [512, 4096] bf16
-        y = torch.randn(BATCH, HQ_TOTAL * HEAD_DIM, device=dev).to(torch.bfloat16)
-        for _ in range(5):
-            dist.all_reduce(y)
-        torch.cuda.synchronize(dev)
-        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a0.record(stream)
-        for _ in range(50):
-            dist.all_reduce(y)
-        a1.record(stream)
-        torch.cuda.synchronize(dev)
-        at = torch.tensor([a0.elapsed_time(a1) / 50], dtype=torch.float64, device=dev)
-        dist.all_reduce(at, op=dist.ReduceOp.MAX)
-        allreduce = {"bytes": y.numel() * 2, "us": round(at.item() * 1e3, 2), "note": "NCCL, outside the timed region"}
-
     if rank == 0:
+        e2e_gbs = (dec_b + store_b) * world / (e2e_ms / 1e3) / 1e9
         line = {"metric": "paged-decode attn HBM GB/s", "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5),
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
                 "data": "synthetic (seeded random bf16 KV cache, q, new k/v)",
                 "config": dict(config_dict(world, ctx), **({"rank_shape": f"one GPU running rank 0's shard of tp{shard}"}
-                                                        if shard != world else {})),
-                "e2e": {"value": round((dec_b + store_b) * world / (e2e_ms / 1e3) / 1e9, 2), "unit": "GB/s",
+                                                        if shard != world else {}),
+                               **({"row_parallel": {"nccl": "NCCL all-reduce of the o_proj output [B, 4096] bf16",
+                                                    "fused": "o_proj GEMM + all-reduce in one kernel "
+                                                             "(OprojAllReduce, peer stores, no multicast)"}[rp]}
+                                  if rp != "none" else {})),
+                "e2e": {"value": round(e2e_gbs, 2), "unit": "GB/s",
                         "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-                        "ms_per_step": round(e2e_ms, 5), "api": "Attention.forward (decode), pinned host buffers"},
+                        "ms_per_step": round(e2e_ms, 5), "wall_ms_per_step": round(wall_ms, 5),
+                        "wall_value": round((dec_b + store_b) * world / (wall_ms / 1e3) / 1e9, 2),
+                        "api": "Attention.forward (decode)" + (" + row-parallel all-reduce" if rp != "none" else "")
+                               + ", pinned host buffers"},
                 "roofline": {"bound": "hbm", "kernel": "paged_attention_kernel", "achieved": round(achieved, 1),
                              "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
-                             "traffic": profiled_traffic(dec_b), "bytes_per_launch": int(dec_b),
-                             "us_per_launch": round(kern_ms * 1e3, 2)},
-                "gpu_launches": 2 * args.steps,
+                             "traffic": round(DRAM_TRAFFIC_RATIO * dec_b),
+                             "traffic_kind": f"scaled: {DRAM_TRAFFIC_RATIO} x algorithmic bytes (ncu, B=64 capture)",
+                             "bytes_per_launch": int(dec_b), "us_per_launch": round(kern_ms * 1e3, 2)},
+                "attention_us": round(kern_ms * 1e3, 2),
+                "gpus_active": gpus_active, "comm_nranks_ok": comm_ok,
+                "gpu_launches": (3 if rp == "fused" else 2) * args.steps,
                 "clocks": clk.summary()}
-        if allreduce:
-            line["allreduce"] = allreduce
+        if rp != "none":
+            line["row_parallel_us"] = round(rp_ms * 1e3, 2)
+            line["row_parallel_bytes"] = BATCH * hidden * 2
+    if world == 1 and not args.no_extras:
+        # the denser configurations of the path, kernels timed alone (1 GPU)
+        n = max(10, min(args.steps, 50))
+        extras = {"prefill_config3": measure_prefill(pkg, torch, dev, n, args.warmup),
+                  "verify_config4": measure_verify(pkg, torch, dev, n, args.warmup)}
+        line.update(extras)
+    if rank == 0:
         if not args.no_cpu_baseline:
             with _all_host_threads():
                 line["cpu_baseline"] = cpu_baseline(ctx, hq, hkv, args.cpu_seconds)
