@@ -62,8 +62,9 @@ enum b200_dtype { B200_F16 = 0, B200_BF16 = 1, B200_F32 = 2 };
 B200_API const char* b200_last_error(void);
 
 /* Bumped whenever a signature below changes (2: b200_oproj_allreduce takes its
- * split-K workspace and low-latency slots; the epoch moved to the device). */
-#define B200_ABI_VERSION 2
+ * split-K workspace and low-latency slots; the epoch moved to the device;
+ * 3: b200_varlen_prefill takes a workspace for its dynamic scheduler). */
+#define B200_ABI_VERSION 3
 B200_API int32_t b200_abi_version(void);
 
 /*
@@ -301,8 +302,14 @@ B200_API int32_t b200_testing_idle_producer(int32_t launches, int64_t wait_limit
  * Hkv, D] and key position p of sequence s lives in block
  * block_tables[s][p / block_size].  Query i of a sequence with Lq queries and
  * Lk keys sees key positions p <= i + Lk - Lq (bottom-right causal mask).
+ * workspace: b200_varlen_prefill_workspace_size() bytes, 256-byte aligned,
+ * zero-filled once before the first call (it holds the work counter that the
+ * CTAs claim query tiles from; every call leaves it zeroed again).  Calls
+ * sharing a workspace must not overlap on the GPU.
  * Constraints: D == 128, dtype bf16 or fp16, block_size % 128 == 0.
  */
+B200_API size_t b200_varlen_prefill_workspace_size(void);
+
 B200_API int32_t b200_varlen_prefill(void* out, const void* q, int64_t q_stride_token,
                             const void* k, int64_t k_stride_token,
                             const void* v, int64_t v_stride_token,
@@ -313,7 +320,8 @@ B200_API int32_t b200_varlen_prefill(void* out, const void* q, int64_t q_stride_
                             const int32_t* block_tables, int32_t block_table_stride,
                             int32_t block_size,
                             int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
-                            float softmax_scale, int32_t dtype, void* stream);
+                            float softmax_scale, int32_t dtype,
+                            void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Copies the prefill kernels' device-side error word to *flag after

@@ -26,8 +26,9 @@ SIGNATURES = {
     "b200_workspace_error": (_I32, [_P, _P, ctypes.POINTER(ctypes.c_int32)]),
     "b200_paged_attention_noalloc_error": (_I32, [_P, ctypes.POINTER(ctypes.c_int32)]),
     "b200_testing_idle_producer": (_I32, [_I32, _I64]),
+    "b200_varlen_prefill_workspace_size": (_SZ, []),
     "b200_varlen_prefill": (_I32, [_P, _P, _I64, _P, _I64, _P, _I64, _P, _P, _I32, _I32, _I32, _I32, _I32, _P,
-                                   _I32, _I32, _I32, _I32, _I32, _F, _I32, _P]),
+                                   _I32, _I32, _I32, _I32, _I32, _F, _I32, _P, _SZ, _P]),
     "b200_varlen_prefill_error": (_I32, [_P, ctypes.POINTER(ctypes.c_int32)]),
     "b200_spec_accept_workspace_size": (_SZ, [_I32, _I32, _I32]),
     "b200_spec_accept": (_I32, [_P, _P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _P, _SZ, _P]),
@@ -42,7 +43,7 @@ SIGNATURES = {
     "b200_qk_norm_rope_store": (_I32, [_P, _I64, _P, _I64, _P, _I64, _P, _P, _P, _F, _P, _I32, _P, _P, _P, _I64,
                                        _I32, _I32, _I32, _I32, _I32, _P]),
 }
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 _lib = None
 _lock = threading.Lock()

@@ -3,11 +3,24 @@
 // nanovllm/layers/attention.py:64-70, with or without a block table (prefix
 // caching / chunked prefill reads keys from the paged cache).
 //
-// Persistent CTAs (one per SM) walk work units -- two 128-query tiles A and B
-// that read the same K/V tiles: the same rows of two query heads of one kv
-// head when the GQA group is even, else rows r and r + 128 of one head --
-// heaviest first.  Tensor memory is allocated once; the K/V rings and every
-// barrier phase run on across units.  Warp roles (three warpgroups):
+// Persistent CTAs (one per SM) walk work units -- two 128-row query tiles A
+// and B that read the same K/V tiles.  When the GQA group is even a unit is
+// 128 query positions of a pair of query heads of one kv head, and each tile
+// holds 64 positions of both heads (rows 0-63 the first head, 64-127 the
+// second): both heads see the same keys, so a sequence's last, partial block
+// of positions fills whole rows of both heads and the diagonal tiles are
+// narrower, which saves 8 % of the tensor work of a prefix-cached prefill
+// batch against one head per tile.  Otherwise a unit is rows r and r + 128
+// of one head.
+// Units are numbered heaviest first and claimed dynamically: the producer
+// takes the next number from an atomic counter in the caller's workspace
+// whenever it is ready for a new unit (numbers past a sequence's queries are
+// skipped) and hands it to the other roles through a two-slot unit ring in
+// shared memory; the last CTA to finish re-arms the counter, so the call is
+// CUDA-graph capturable.  Dynamic claiming keeps the SMs evenly loaded where a
+// static assignment left a quarter of their time idle.  Tensor memory is
+// allocated once; the K/V rings and every barrier phase run on across units.
+// Warp roles (three warpgroups):
 //   warps 0-3 / 4-7  softmax of tile A / B, one thread per query row (TMEM
 //             lane = row), and the epilogue O / l -> out;
 //   warp 8    producer: TMA loads (no multicast) of both Q tiles and of
@@ -58,6 +71,10 @@ constexpr uint32_t kColS = 0;
 constexpr uint32_t kColP = 128;  // + 64 * t
 constexpr uint32_t kColO = 256;  // + 128 * t
 constexpr float kRescaleLog2 = 8.0f;
+constexpr int kUnitRing = 2;  // claimed units in flight between the producer and the other roles
+// Readers of each unit-ring slot: the V loader lane, the two MMA issuers, the eight softmax warps.
+constexpr int kUnitReaders = 1 + 2 + 8;
+constexpr size_t kWorkspaceBytes = 256;  // [0] next unit, [1] finished CTAs
 
 struct Params {
     uint16_t* out;
@@ -67,9 +84,11 @@ struct Params {
     const int32_t* block_tables;
     int32_t bt_stride, block_size, num_blocks;
     int32_t num_seqs, hq, hkv, group, q_blocks;
-    int32_t pair;   // 1: tiles A/B are two query heads of one kv head (even group); 0: rows r / r+128 of one head
+    int32_t pair;   // 1: tile A/B = positions 0-63 / 64-127 of a unit's block, each for two query heads of one
+                    //    kv head (even group; rows 0-63 the first head, 64-127 the second); 0: rows r / r+128 of one head
     int32_t slots;  // head slots per sequence: hq / 2 when pairing, else hq
     float scale_log2;
+    int32_t* sched;  // caller workspace: [0] next unit to claim, [1] CTAs finished
 };
 
 struct Smem {
@@ -82,6 +101,8 @@ struct Smem {
     uint64_t s_full[2], p_ready[2], o_done[2];  // per tile A/B
     uint64_t s_free;                            // the S buffer has been read (one phase per S tile)
     uint64_t drain;
+    uint64_t unit_full[kUnitRing], unit_empty[kUnitRing];
+    int32_t unit_ring[kUnitRing];               // claimed unit numbers, -1 = no more units
     uint32_t tmem_base;
     int32_t err;
 };
@@ -105,46 +126,48 @@ __device__ __forceinline__ int key_tiles(int r0, int r1, int lq, int lk) {
 }
 
 // One work unit: two 128-row query tiles A and B of one sequence that read the
-// same K/V tiles -- the same rows of two query heads of one kv head when the
-// group is even (both tiles see the same keys), else rows r and r + 128 of
-// one head.
+// same K/V tiles -- positions row[t] .. row[t] + 63 of the heads h[t] and
+// h[t] + 1 of one kv head when the group is even, else positions row[t] ..
+// row[t] + 127 of head h[t].
+// Per-tile fields are scalars with select accessors (no arrays), so that a
+// runtime tile index never forces the unit into local memory.
 struct Unit {
-    int s, q0, lq, k0, lk, h[2], row[2], nt[2], ntiles;
+    int s, q0, lq, k0, lk, h0, h1, row0, row1, nt0, nt1, ntiles;
     bool has_b;
+    __device__ __forceinline__ int h(int t) const { return t ? h1 : h0; }
+    __device__ __forceinline__ int row(int t) const { return t ? row1 : row0; }
+    __device__ __forceinline__ int nt(int t) const { return t ? nt1 : nt0; }
 };
 
 // Units are numbered heaviest first (later query blocks see more keys), then by
 // sequence and head; returns false for blocks past the sequence's queries.
-// CTA c takes the units at positions i with snake(i) == c, where positions run
-// c, then 2G-1-c, then 2G+c, ... (boustrophedon), which balances the static
-// assignment of units of decreasing cost.
-__device__ __forceinline__ int unit_at(int k, int cta, int G) {
-    return (k & 1) ? (k + 1) * G - 1 - cta : k * G + cta;
-}
 __device__ __forceinline__ bool load_unit(const Params& p, int u, Unit& w) {
     const int per = p.num_seqs * p.slots;
     const int qb = p.q_blocks - 1 - u / per;
     const int rem = u - (u / per) * per;
     w.s = rem / p.slots;
     const int hs = rem - w.s * p.slots;
+    int span;  // query positions per tile
     if (p.pair) {
-        w.h[0] = 2 * hs;
-        w.h[1] = 2 * hs + 1;
-        w.row[0] = w.row[1] = qb * kBM;
+        w.h0 = w.h1 = 2 * hs;  // first head of the pair; rows 64-127 of a tile are head 2 * hs + 1
+        w.row0 = qb * kBM;
+        w.row1 = w.row0 + kBM / 2;
+        span = kBM / 2;
     } else {
-        w.h[0] = w.h[1] = hs;
-        w.row[0] = qb * 2 * kBM;
-        w.row[1] = w.row[0] + kBM;
+        w.h0 = w.h1 = hs;
+        w.row0 = qb * 2 * kBM;
+        w.row1 = w.row0 + kBM;
+        span = kBM;
     }
     w.q0 = p.cu_q[w.s];
     w.lq = p.cu_q[w.s + 1] - w.q0;
-    if (w.row[0] >= w.lq) return false;
+    if (w.row0 >= w.lq) return false;
     w.k0 = p.cu_k[w.s];
     w.lk = p.cu_k[w.s + 1] - w.k0;
-    w.nt[0] = key_tiles(w.row[0], w.row[0] + kBM, w.lq, w.lk);
-    w.nt[1] = key_tiles(w.row[1], w.row[1] + kBM, w.lq, w.lk);
-    w.ntiles = max(w.nt[0], w.nt[1]);
-    w.has_b = w.row[1] < w.lq;
+    w.nt0 = key_tiles(w.row0, w.row0 + span, w.lq, w.lk);
+    w.nt1 = key_tiles(w.row1, w.row1 + span, w.lq, w.lk);
+    w.ntiles = max(w.nt0, w.nt1);
+    w.has_b = w.row1 < w.lq;
     return true;
 }
 
@@ -154,6 +177,23 @@ __device__ __forceinline__ bool load_unit(const Params& p, int u, Unit& w) {
 // P = 2^(S*scale - m) is packed to bf16 pairs in pk for the caller to store.
 // `mask` applies the bottom-right causal / sequence-end masking (diagonal and
 // tail tiles only).
+// The next claimed unit from the ring (n counts the units this role has
+// taken); -1 when there are no more, -2 when the wait ran out.  Called by one
+// thread of a role, or by a whole warp (then every lane reads and lane 0
+// releases the slot after the warp has read it).
+__device__ __forceinline__ int take_unit(Smem& sm, int& n, bool warp_reader) {
+    const int slot = n % kUnitRing;
+    const uint32_t parity = (n / kUnitRing) & 1;
+    bool ok = mbar_wait(&sm.unit_full[slot], parity);
+    if (warp_reader) ok = __all_sync(0xffffffffu, ok);
+    if (!ok) return -2;
+    const int u = *reinterpret_cast<volatile int32_t*>(&sm.unit_ring[slot]);
+    if (warp_reader) __syncwarp();
+    if (!warp_reader || (threadIdx.x & 31) == 0) mbar_arrive(&sm.unit_empty[slot]);
+    ++n;
+    return u;
+}
+
 template <bool BF16>
 __device__ __forceinline__ void softmax_tile(bool mask, uint32_t s_col, uint64_t* s_free, int kbase, int limit,
                                              float sl2, float& m, float& alpha, bool& rescale, float& sum,
@@ -212,6 +252,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int total_units = p.q_blocks * p.num_seqs * p.slots;
 
     if (tid == 0) {
+        for (int i = 0; i < kUnitRing; ++i) {
+            mbar_init(&sm.unit_full[i], 1);
+            mbar_init(&sm.unit_empty[i], kUnitReaders);
+        }
         mbar_init(&sm.q_full, 1);
         mbar_init(&sm.q_empty, 1);
         for (int i = 0; i < kKStages; ++i) {
@@ -264,23 +308,55 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint64_t* empty = kq ? sm.k_empty : sm.v_empty;
                 const CUtensorMap* tm = kq ? &tmk : &tmv;
                 int nq = 0, g = 0;  // units loaded, tiles loaded (across units)
+                int nu = 0;         // units pushed into (lane 0) or taken from (lane 1) the ring
                 Unit w;
-                for (int k = 0;; ++k) {
-                    const int u = unit_at(k, blockIdx.x, gridDim.x);
-                    if (u >= total_units || failed()) break;
-                    if (!load_unit(p, u, w) || w.ntiles == 0) continue;
+                while (!failed()) {
+                    int u;
+                    if (kq) {
+                        // claim the next unit that has query rows, and hand it to the other roles
+                        do {
+                            u = atomicAdd(&p.sched[0], 1);
+                        } while (u < total_units && !load_unit(p, u, w));
+                        if (u >= total_units) u = -1;
+                        const int slot = nu % kUnitRing;
+                        if (!wait_or_flag(&sm.unit_empty[slot], ((nu / kUnitRing) & 1) ^ 1, sm)) break;
+                        sm.unit_ring[slot] = u;
+                        mbar_arrive(&sm.unit_full[slot]);
+                        ++nu;
+                    } else {
+                        u = take_unit(sm, nu, false);
+                        if (u == -2) {
+                            atomicOr(&g_prefill_error, 1);
+                            *reinterpret_cast<volatile int32_t*>(&sm.err) = 1;
+                            break;
+                        }
+                        if (u >= 0) load_unit(p, u, w);
+                    }
+                    if (u < 0) break;
+                    if (w.ntiles == 0) continue;
                     if (kq) {
                         // Q of the previous unit must no longer be read by S MMAs.
                         if (!wait_or_flag(&sm.q_empty, (nq & 1) ^ 1, sm)) break;
                         mbar_arrive_expect_tx(&sm.q_full, (w.has_b ? 4 : 2) * kHalf);
                         for (int t = 0; t < (w.has_b ? 2 : 1); ++t) {
-                            tma_load_2d(sm.q[t][0], &tmq, w.h[t] * kD, w.q0 + w.row[t], &sm.q_full, pol_q);
-                            tma_load_2d(sm.q[t][1], &tmq, w.h[t] * kD + 64, w.q0 + w.row[t], &sm.q_full, pol_q);
+                            if (p.pair) {
+                                // two 64-row boxes per 64-dim half: the pair's heads, 8 KiB apart
+                                for (int hh = 0; hh < 2; ++hh) {
+                                    const int x = (w.h(t) + hh) * kD;
+                                    tma_load_2d(sm.q[t][0] + hh * (kHalf / 2), &tmq, x, w.q0 + w.row(t), &sm.q_full,
+                                                pol_q);
+                                    tma_load_2d(sm.q[t][1] + hh * (kHalf / 2), &tmq, x + 64, w.q0 + w.row(t),
+                                                &sm.q_full, pol_q);
+                                }
+                            } else {
+                                tma_load_2d(sm.q[t][0], &tmq, w.h(t) * kD, w.q0 + w.row(t), &sm.q_full, pol_q);
+                                tma_load_2d(sm.q[t][1], &tmq, w.h(t) * kD + 64, w.q0 + w.row(t), &sm.q_full, pol_q);
+                            }
                         }
                         ++nq;
                     }
                     const int32_t* bt = p.block_tables ? p.block_tables + int64_t(w.s) * p.bt_stride : nullptr;
-                    const int x = (w.h[0] / p.group) * kD;
+                    const int x = (w.h0 / p.group) * kD;
                     for (int j = 0; j < w.ntiles; ++j, ++g) {
                         const int st = g % NS;
                         if (failed() || !wait_or_flag(&empty[st], ((g / NS) & 1) ^ 1, sm)) break;
@@ -323,12 +399,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                 int nq = 0, g = 0;
                 int n_s = 0;              // S tiles issued (across units): the S buffer's uses
                 int npv[2] = {0, 0};      // PV tiles issued per query tile (across units)
+                int nu = 0;               // units taken from the ring
                 bool ok = true;
                 Unit w;
-                for (int k = 0; ok; ++k) {
-                    const int u = unit_at(k, blockIdx.x, gridDim.x);
-                    if (u >= total_units || failed()) break;
-                    if (!load_unit(p, u, w) || w.ntiles == 0) continue;
+                while (ok && !failed()) {
+                    const int u = take_unit(sm, nu, false);
+                    if (u == -2) {
+                        atomicOr(&g_prefill_error, 1);
+                        *reinterpret_cast<volatile int32_t*>(&sm.err) = 1;
+                        break;
+                    }
+                    if (u < 0) break;
+                    load_unit(p, u, w);
+                    if (w.ntiles == 0) continue;
                     const int g0 = g;
                     if (s_issuer) {
                         if (!wait_or_flag(&sm.q_full, nq & 1, sm)) { ok = false; break; }
@@ -340,7 +423,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             tc::fence_after_sync();
                             const uint32_t ka = smem_u32(sm.k[kst][0]);
                             for (int t = 0; t < 2; ++t) {
-                                if (j >= w.nt[t]) continue;
+                                if (j >= w.nt(t)) continue;
                                 // the previous S tile must have been read out of the buffer
                                 if (n_s > 0 && !wait_or_flag(&sm.s_free, (n_s - 1) & 1, sm)) { ok = false; break; }
                                 ++n_s;
@@ -365,7 +448,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             if (!wait_or_flag(&sm.v_full[vst], (gj / kVStages) & 1, sm)) { ok = false; break; }
                             const uint32_t va = smem_u32(sm.v[vst][0]);
                             for (int t = 0; t < 2; ++t) {
-                                if (j >= w.nt[t]) continue;
+                                if (j >= w.nt(t)) continue;
                                 if (!wait_or_flag(&sm.p_ready[t], npv[t] & 1, sm)) { ok = false; break; }
                                 ++npv[t];
                                 tc::fence_after_sync();
@@ -404,16 +487,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float sl2 = p.scale_log2;
         int ns = 0;  // S tiles of this query tile consumed (across units) = P tiles written
         int g = 0;   // K/V tiles streamed so far (across units), to find a tile's stage
+        int nu = 0;  // units taken from the ring
         Unit w;
-        for (int k = 0;; ++k) {
-            const int u = unit_at(k, blockIdx.x, gridDim.x);
-            if (u >= total_units || failed()) break;
-            if (!load_unit(p, u, w)) continue;
+        while (!failed()) {
+            const int u = take_unit(sm, nu, true);
+            if (u == -2) {
+                if (lane == 0) atomicOr(&g_prefill_error, 1);
+                *reinterpret_cast<volatile int32_t*>(&sm.err) = 1;
+                break;
+            }
+            if (u < 0) break;
+            load_unit(p, u, w);
             const int g0 = g;
             g += w.ntiles;
-            const int qrow = w.row[t] + r;
-            const int my_tiles = w.nt[t];
-            uint4* dst = reinterpret_cast<uint4*>(p.out + int64_t(w.q0 + qrow) * p.out_stride + w.h[t] * kD);
+            // this thread's query row: position and head
+            const int qrow = p.pair ? w.row(t) + (r & (kBM / 2 - 1)) : w.row(t) + r;
+            const int qhead = p.pair ? w.h(t) + (r >> 6) : w.h(t);
+            const int my_tiles = w.nt(t);
+            uint4* dst = reinterpret_cast<uint4*>(p.out + int64_t(w.q0 + qrow) * p.out_stride + qhead * kD);
             if (my_tiles == 0) {  // rows that see no key at all (only when lk < lq)
                 if (qrow < w.lq)
                     for (int c = 0; c < kD / 8; ++c) dst[c] = make_uint4(0, 0, 0, 0);
@@ -460,7 +551,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc::tmem_wait_st();
                 // Cache rows past this sequence's keys may hold NaN bits; P is 0 there but
                 // 0 * NaN is NaN, so the first tile to use the stage clears those V rows.
-                if (kbase + kBN > w.lk && (t == 0 || j >= w.nt[0])) {
+                if (kbase + kBN > w.lk && (t == 0 || j >= w.nt0)) {
                     const int gj = g0 + j, st = gj % kVStages;
                     if (!wait_or_flag(&sm.v_full[st], (gj / kVStages) & 1, sm)) { ok = false; break; }
                     if (kbase + r >= w.lk) {
@@ -507,6 +598,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::fence_after_sync();
         tc::tmem_dealloc(tmem, kTmemCols);
     }
+    if (tid == 0) {
+        __threadfence();
+        const int done = atomicAdd(&p.sched[1], 1);
+        if (done == int(gridDim.x) - 1) {
+            // Every CTA has stopped claiming units: re-arm the counter for the next call.
+            atomicExch(&p.sched[0], 0);
+            atomicExch(&p.sched[1], 0);
+        }
+    }
 }
 
 }  // namespace pf
@@ -519,7 +619,7 @@ extern "C" int32_t b200_varlen_prefill(void* out, const void* q, int64_t q_strid
                                        int32_t total_k_rows,
                                        const int32_t* block_tables, int32_t block_table_stride, int32_t block_size,
                                        int32_t num_heads, int32_t num_kv_heads, int32_t head_dim, float softmax_scale,
-                                       int32_t dtype, void* stream) {
+                                       int32_t dtype, void* workspace, size_t workspace_bytes, void* stream) {
     using namespace b200;
     using namespace b200::pf;
     clear_error();
@@ -537,14 +637,18 @@ extern "C" int32_t b200_varlen_prefill(void* out, const void* q, int64_t q_strid
                      v_stride_token >= int64_t(num_kv_heads) * kD,
                  "varlen_prefill: token strides below the head rows");
     B200_REQUIRE((reinterpret_cast<uintptr_t>(out) & 15) == 0, "varlen_prefill: out must be 16-byte aligned");
+    if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255) || workspace_bytes < kWorkspaceBytes)
+        return fail(B200_ERR_WORKSPACE, "varlen_prefill: workspace missing, unaligned or smaller than %zu bytes",
+                    kWorkspaceBytes);
     if (block_tables) {
         B200_REQUIRE(block_size > 0 && block_size % kBN == 0, "varlen_prefill: block_size %d not a multiple of %d",
                      block_size, kBN);
         B200_REQUIRE(block_table_stride > 0, "varlen_prefill: block_table_stride %d", block_table_stride);
         B200_REQUIRE(total_k_rows % block_size == 0, "varlen_prefill: cache rows %d not whole blocks", total_k_rows);
     }
-    // Even GQA groups pair two query heads per unit (same rows, same keys: the
-    // tiles stay in step); otherwise a unit is 256 rows of one head.
+    // Even GQA groups pair two query heads per unit (128 positions; each tile
+    // holds 64 positions of both heads, which see the same keys); otherwise a
+    // unit is 256 rows of one head.
     const int group = num_heads / num_kv_heads;
     const bool pair = group % 2 == 0;
     const int slots = pair ? num_heads / 2 : num_heads;
@@ -559,8 +663,8 @@ extern "C" int32_t b200_varlen_prefill(void* out, const void* q, int64_t q_strid
     // outside the buffers; such rows are masked and never stored.
     CUtensorMap tmq, tmk, tmv;
     const uint64_t q_rows = uint64_t(total_q);
-    int32_t rc = make_tmap_2d(&tmq, q, uint64_t(num_heads) * kD, q_rows, uint64_t(q_stride_token) * 2, 64, kBM, bf16,
-                              CU_TENSOR_MAP_SWIZZLE_128B);
+    int32_t rc = make_tmap_2d(&tmq, q, uint64_t(num_heads) * kD, q_rows, uint64_t(q_stride_token) * 2, 64,
+                              pair ? kBM / 2 : kBM, bf16, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
     rc = make_tmap_2d(&tmk, k, uint64_t(num_kv_heads) * kD, uint64_t(total_k_rows), uint64_t(k_stride_token) * 2, 64,
                       kBN, bf16, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -586,6 +690,7 @@ extern "C" int32_t b200_varlen_prefill(void* out, const void* q, int64_t q_strid
     prm.pair = pair ? 1 : 0;
     prm.slots = slots;
     prm.scale_log2 = softmax_scale * 1.4426950408889634f;
+    prm.sched = static_cast<int32_t*>(workspace);
 
     const int smem = int(sizeof(Smem)) + 1024;
     const void* fn = bf16 ? (const void*)prefill_kernel<true> : (const void*)prefill_kernel<false>;
@@ -598,6 +703,8 @@ extern "C" int32_t b200_varlen_prefill(void* out, const void* q, int64_t q_strid
     B200_CUDA_TRY(cudaGetLastError());
     return B200_OK;
 }
+
+extern "C" size_t b200_varlen_prefill_workspace_size(void) { return b200::pf::kWorkspaceBytes; }
 
 extern "C" int32_t b200_varlen_prefill_error(void* stream, int32_t* flag) {
     using namespace b200;

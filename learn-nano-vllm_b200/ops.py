@@ -157,6 +157,21 @@ def workspace_error(workspace: torch.Tensor) -> int:
 
 
 # ------------------------------------------------------------ varlen prefill
+_prefill_workspaces: dict[int, torch.Tensor] = {}
+
+
+def prefill_workspace(device: torch.device) -> torch.Tensor:
+    """Per-device workspace of the prefill kernel (its work counter; zero-filled once)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    with _ws_lock:
+        ws = _prefill_workspaces.get(idx)
+        if ws is None:
+            n = max(int(lib().b200_varlen_prefill_workspace_size()), 256)
+            ws = torch.zeros(n, dtype=torch.uint8, device=torch.device("cuda", idx))
+            _prefill_workspaces[idx] = ws
+    return ws
+
+
 def flash_attn_varlen_func(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k, softmax_scale=None,
                            causal=True, block_table=None, out=None):
     """Drop-in for the prefill call of nanovllm/layers/attention.py:67-70.
@@ -192,10 +207,12 @@ def flash_attn_varlen_func(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, ma
     scale = D ** -0.5 if softmax_scale is None else softmax_scale
     if Tq == 0 or S == 0:
         return out
+    ws = prefill_workspace(q.device)
     rc = lib().b200_varlen_prefill(out.data_ptr(), q.data_ptr(), q.stride(0), k.data_ptr(), k_stride, v.data_ptr(),
                                    v_stride, cu_seqlens_q.data_ptr(), cu_seqlens_k.data_ptr(), S, Tq,
                                    int(max_seqlen_q), int(max_seqlen_k), total_k_rows, bt_ptr, bt_stride, bs,
-                                   Hq, Hkv, D, float(scale), _DTYPES[q.dtype], _stream(q))
+                                   Hq, Hkv, D, float(scale), _DTYPES[q.dtype], ws.data_ptr(), ws.numel(),
+                                   _stream(q))
     check(rc, "varlen_prefill")
     return out
 
