@@ -58,7 +58,7 @@ FALLBACK_BF16_TFLOPS = 1590.0
 # -k regex:paged_attention -s 2 -c 1 python bench.py --batch 64 --steps 3 --warmup 1
 # --no-cpu-baseline --no-extras); the full launch is too large to capture with every metric,
 # and its traffic grows in proportion (K/V rows are read once), so traffic is reported scaled.
-DRAM_TRAFFIC_RATIO = 1.034
+DRAM_TRAFFIC_RATIO = 1.033
 
 
 def parse():
@@ -947,33 +947,78 @@ def main():
     d_bt, d_cl, d_sl = torch.empty_like(bt), torch.empty_like(cl), torch.empty_like(slots)
     h2d = sum(t.numel() * t.element_size() for t in (h_q, h_k, h_v, h_bt, h_cl, h_sl))
     d2h = h_out.numel() * h_out.element_size()
+    hosts = (h_q, h_k, h_v, h_bt, h_cl, h_sl)
 
-    def e2e_step():
-        for d, h in ((d_q, h_q), (d_k, h_k), (d_v, h_v), (d_bt, h_bt), (d_cl, h_cl), (d_sl, h_sl)):
-            d.copy_(h, non_blocking=True)
-        pctx.set_context(False, slot_mapping=d_sl, context_lens=d_cl, block_tables=d_bt)
-        o = attn(d_q, d_k, d_v)
+    def layer(b):
+        pctx.set_context(False, slot_mapping=b[5], context_lens=b[4], block_tables=b[3])
+        o = attn(b[0], b[1], b[2])
         if rp == "nccl":
             dist.all_reduce(y)
         elif rp == "fused":
             oproj(o.view(BATCH, hq * HEAD_DIM), wo, out=y)
-        h_out.copy_(o, non_blocking=True)
+        return o
 
-    for _ in range(3):
-        e2e_step()
+    serial_bufs = (d_q, d_k, d_v, d_bt, d_cl, d_sl)
+
+    def e2e_serial(n):
+        """Each step copies its inputs up, computes and copies the output back, in order on one stream."""
+        for _ in range(n):
+            for d, h in zip(serial_bufs, hosts):
+                d.copy_(h, non_blocking=True)
+            o = layer(serial_bufs)
+            h_out.copy_(o, non_blocking=True)
+
+    # As a serving loop runs it: step i+1's inputs are copied up on a second stream while step i
+    # computes, and step i's output is copied back on that stream as soon as step i is done.
+    cs = torch.cuda.Stream(dev)
+    bufs = [serial_bufs, tuple(torch.empty_like(d) for d in serial_bufs)]
+    h_outs = [h_out, torch.empty(out.shape, dtype=out.dtype).pin_memory()]
+
+    def e2e_pipelined(n):
+        ev_up = [torch.cuda.Event(), torch.cuda.Event()]
+        ev_done = [torch.cuda.Event(), torch.cuda.Event()]
+        cs.wait_stream(stream)
+        with torch.cuda.stream(cs):
+            for d, h in zip(bufs[0], hosts):
+                d.copy_(h, non_blocking=True)
+            ev_up[0].record(cs)
+        for i in range(n):
+            j = i & 1
+            stream.wait_event(ev_up[j])
+            o = layer(bufs[j])
+            ev_done[j].record(stream)
+            with torch.cuda.stream(cs):
+                if i + 1 < n:
+                    if i >= 1:  # the other buffer set was read by step i - 1
+                        cs.wait_event(ev_done[j ^ 1])
+                    for d, h in zip(bufs[j ^ 1], hosts):
+                        d.copy_(h, non_blocking=True)
+                    ev_up[j ^ 1].record(cs)
+                cs.wait_event(ev_done[j])
+                o.record_stream(cs)
+                h_outs[j].copy_(o, non_blocking=True)
+        stream.wait_stream(cs)
+
+    def timed_e2e(fn, n):
+        """Device time (events on the compute stream, which waits for the copy stream at the end)
+        and wall-clock time per step."""
+        torch.cuda.synchronize(dev)
+        barrier()
+        x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        w0 = time.perf_counter()
+        x0.record(stream)
+        fn(n)
+        x1.record(stream)
+        torch.cuda.synchronize(dev)
+        wall = (time.perf_counter() - w0) * 1e3 / n
+        barrier()
+        return x0.elapsed_time(x1) / n, wall
+
+    e2e_serial(3)
+    e2e_pipelined(3)
     ne = max(10, min(args.steps, 200))
-    torch.cuda.synchronize(dev)
-    barrier()
-    x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    w0 = time.perf_counter()
-    x0.record(stream)
-    for _ in range(ne):
-        e2e_step()
-    x1.record(stream)
-    torch.cuda.synchronize(dev)
-    wall_ms = (time.perf_counter() - w0) * 1e3 / ne
-    barrier()
-    e2e_ms = x0.elapsed_time(x1) / ne
+    serial_ms, serial_wall_ms = timed_e2e(e2e_serial, ne)
+    e2e_ms, wall_ms = timed_e2e(e2e_pipelined, ne)
     pctx.reset_context()
 
     # every rank on its own GPU, every rank in the communicator
@@ -987,10 +1032,11 @@ def main():
         comm_ok = int(one.item()) == world == dist.get_world_size()
 
     dec_b, store_b = step_bytes(ctx, hq, hkv, width)
-    t = torch.tensor([ms, kern_ms, e2e_ms, rp_ms, wall_ms], dtype=torch.float64, device=dev)
+    t = torch.tensor([ms, kern_ms, e2e_ms, rp_ms, wall_ms, serial_ms, serial_wall_ms], dtype=torch.float64,
+                     device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, kern_ms, e2e_ms, rp_ms, wall_ms = t.tolist()
+    ms, kern_ms, e2e_ms, rp_ms, wall_ms, serial_ms, serial_wall_ms = t.tolist()
     if oproj is not None:
         torch.cuda.synchronize(dev)
         barrier()
@@ -1017,7 +1063,11 @@ def main():
                         "ms_per_step": round(e2e_ms, 5), "wall_ms_per_step": round(wall_ms, 5),
                         "wall_value": round((dec_b + store_b) * world / (wall_ms / 1e3) / 1e9, 2),
                         "api": "Attention.forward (decode)" + (" + row-parallel all-reduce" if rp != "none" else "")
-                               + ", pinned host buffers"},
+                               + ", pinned host buffers; step i+1's inputs copied up on a second stream while "
+                                 "step i computes, step i's output copied back behind it",
+                        "serial": {"value": round((dec_b + store_b) * world / (serial_ms / 1e3) / 1e9, 2),
+                                   "ms_per_step": round(serial_ms, 5), "wall_ms_per_step": round(serial_wall_ms, 5),
+                                   "note": "copy up, compute, copy back in order on one stream"}},
                 "roofline": {"bound": "hbm", "kernel": "paged_attention_kernel", "achieved": round(achieved, 1),
                              "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
                              "traffic": round(DRAM_TRAFFIC_RATIO * dec_b),
