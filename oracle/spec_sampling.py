@@ -20,13 +20,14 @@ exponential race rather than an inverse CDF, so that step is pinned in distribut
 Every floating-point operation is defined in a fixed order with float32
 rounding, so that the CUDA kernel reproduces the decisions and the sampled
 tokens bit for bit given identical uniforms:
-  * exp_c (for x <= 0): y = min(x*log2(e), 0); n = rint(y) by the magic
+  * exp_c (for x <= 0): y = x*log2(e); n = rint(y) by the magic
     constant 1.5*2^23 (t = y + c, n = t - c, round to nearest even);
     f = y - n; P(f) = a degree-5 polynomial for 2^f on [-1/2, 1/2] (the
     minimax fit of the relative error with P(0) = 1, by linear programming,
     1.6e-7 at most in float32; coefficients EXP2_COEF) by Horner with fused
     multiply-add (one rounding per step);
-    exp_c = P * 2^n (exponent field add), 0 below y = -125;
+    exp_c = P * 2^n (exponent field add), 0 unless y >= -125 (so 0 for
+    NaN and -inf as well);
   * probabilities: p_j = exp_c(x_j - M) * r with r = 1 / S rounded once;
   * sums: the vocabulary is cut into tiles of 4096; in a tile, "thread" i
     (0..255) adds its 16 elements k*1024 + 4*i + c (k = 0..3 outer,
@@ -92,17 +93,19 @@ MAGIC = f32(12582912.0)  # 1.5 * 2^23
 def exp_c(x):
     """exp(x) for float32 x <= 0 with the fixed operation order above."""
     x = np.asarray(x, dtype=f32)
-    y = np.minimum((x * LOG2E).astype(f32), f32(0.0))
-    t = (y + MAGIC).astype(f32)
-    n = (t - MAGIC).astype(f32)
-    fr = (y - n).astype(f32)
-    p = np.full_like(fr, EXP2_COEF[-1])
-    for c in EXP2_COEF[-2::-1]:
-        p = fma32(p, fr, c)
-    ni = np.where(y < f32(-125.0), 0, n).astype(np.int32)
-    bits = (p.view(np.int32) + (ni << np.int32(23))).astype(np.int32)
-    r = bits.view(f32)
-    return np.where(y < f32(-125.0), f32(0.0), r).astype(f32)
+    with np.errstate(invalid="ignore"):
+        y = (x * LOG2E).astype(f32)
+        t = (y + MAGIC).astype(f32)
+        n = (t - MAGIC).astype(f32)
+        fr = (y - n).astype(f32)
+        p = np.full_like(fr, EXP2_COEF[-1])
+        for c in EXP2_COEF[-2::-1]:
+            p = fma32(p, fr, c)
+        keep = y >= f32(-125.0)  # False for NaN and -inf too: those give 0
+        ni = np.where(keep, n, f32(0.0)).astype(np.int32)
+        bits = (p.view(np.int32) + (ni << np.int32(23))).astype(np.int32)
+        r = bits.view(f32)
+        return np.where(keep, r, f32(0.0)).astype(f32)
 
 
 def exp2_coef_hex():

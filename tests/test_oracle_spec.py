@@ -131,3 +131,17 @@ def test_exp2_coefficients_come_from_their_generator():
     assert lits == [float(c) for c in want]
     _, t = gen.fit()
     assert t < 1e-7
+
+
+def test_exp_c_special_values():
+    """exp_c is 0 for NaN, -inf and anything below 2^-125, exactly 1 at 0, and within the fit's
+    error elsewhere on its domain (x <= 0)."""
+    x = np.asarray([np.nan, -np.inf, -200.0, -86.7, 0.0, -0.0, -1e-30, -0.5, -10.0], np.float32)
+    e = ss.exp_c(x)
+    assert e[0] == 0 and e[1] == 0 and e[2] == 0 and e[3] == 0
+    assert e[4] == 1 and e[5] == 1 and e[6] == 1
+    xs = -np.random.default_rng(0).exponential(8.0, 20000).astype(np.float32)
+    xs = xs[xs > -80]
+    rel = np.abs(ss.exp_c(xs).astype(np.float64) / np.exp(xs.astype(np.float64)) - 1)
+    # fit error plus the float32 rounding of y = x * log2(e), whose absolute error grows with |x|
+    assert (rel <= 3e-7 + np.abs(xs) * 1.2e-7).all()

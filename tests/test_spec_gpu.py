@@ -67,3 +67,16 @@ def test_config4_full_size_bit_exact(pkg, name):
     wt, wn = ss.spec_accept_ref(c.target_logits[rows], c.draft_logits[rows], c.draft_tokens[rows], c.u_accept[rows],
                                 c.u_sample[rows], None)
     assert np.array_equal(num[rows], wn) and np.array_equal(toks[rows], wt)
+
+
+def test_non_finite_logits_weigh_zero(pkg):
+    """NaN and -inf logits (masked vocabulary entries) weigh 0 on both sides, bit for bit."""
+    c = cases.make_spec_case(8, 3, 5000, seed=12)
+    rng = np.random.default_rng(3)
+    for arr in (c.target_logits, c.draft_logits):
+        flat = arr.reshape(-1)
+        idx = rng.choice(flat.size, 400, replace=False)
+        flat[idx[:200]] = -np.inf
+        flat[idx[200:]] = np.nan
+    toks, num, wt, wn = run(pkg, c)
+    assert np.array_equal(num, wn) and np.array_equal(toks, wt)
