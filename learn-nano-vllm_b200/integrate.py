@@ -61,7 +61,10 @@ class _RowParallelState:
     """The fused GEMM + all-reduce buffers of this process, one per (output size, device),
     shared by every RowParallelLinear (they run one after another on one stream)."""
     ops = {}
-    max_tokens = 16384  # nano-vLLM's default max_num_batched_tokens; larger batches use the stock path
+    # Decode-sized batches only (nano-vLLM captures decode graphs up to 512 sequences): there the
+    # fused kernel beats F.linear + NCCL (1.15-1.6x at TP2); prefill batches of thousands of rows
+    # run its GEMM below cuBLAS, so they take the stock path.
+    max_tokens = 512
 
     @classmethod
     def get(cls, n, device):
