@@ -627,7 +627,86 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     if (sm.flag) {
-                        const int full = hd.nchunks - (seq_chunks(hd.ctx, cap, chunk).rem);
+                        const int nch = hd.nchunks;
+                        const int full = nch - (seq_chunks(hd.ctx, cap, chunk).rem);
+                        // The combine buffer is free here: it holds the chunks' weights.
+                        float* wbuf = &sm.co[0][0][0];
+                        constexpr int kWCap = (kConsumerWarps / 2) * RC * kD;
+                        if (nch * p.rows <= kWCap) {
+                            // (1) every chunk's log-sum-exp of every row, all loads in flight at once
+                            for (int i = tid; i < nch * p.rows; i += kConsumers) {
+                                const int c = i / p.rows, r = i - c * p.rows;
+                                const int64_t it = int64_t(chunk_slot(hd.slot0, c, full, total_full)) * p.hkv + hd.h;
+                                wbuf[i] = __ldcg(p.part_lse + it * p.rows + r);
+                            }
+                            if (!consumer_sync(&sm.cbar, cphase, p.wait_ns)) {
+                                atomicOr(&p.ctrl[2], DEV_ERR_WAIT_PEER);
+                                *reinterpret_cast<volatile int32_t*>(&sm.err) = 1;
+                                break;
+                            }
+                            // (2) per row, one warp: weights 2^(lse_c - L) / sum_c, in place
+                            for (int r = warp; r < p.rows; r += kConsumerWarps) {
+                                float L = -INFINITY;
+                                for (int c = lane; c < nch; c += 32) L = fmaxf(L, wbuf[c * p.rows + r]);
+#pragma unroll
+                                for (int o = 16; o >= 1; o >>= 1) L = fmaxf(L, __shfl_xor_sync(0xffffffffu, L, o));
+                                float den = 0.f;
+                                for (int c = lane; c < nch; c += 32) {
+                                    const float w = L == -INFINITY ? 0.f : fast_exp2(wbuf[c * p.rows + r] - L);
+                                    wbuf[c * p.rows + r] = w;
+                                    den += w;
+                                }
+#pragma unroll
+                                for (int o = 16; o >= 1; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
+                                const float inv = den > 0.f ? 1.f / den : 0.f;
+                                for (int c = lane; c < nch; c += 32) wbuf[c * p.rows + r] *= inv;
+                            }
+                            if (!consumer_sync(&sm.cbar, cphase, p.wait_ns)) {
+                                atomicOr(&p.ctrl[2], DEV_ERR_WAIT_PEER);
+                                *reinterpret_cast<volatile int32_t*>(&sm.err) = 1;
+                                break;
+                            }
+                            // (3) outputs: up to kElems elements per thread, the partials of four
+                            // chunks per element loaded together (independent L2 reads in flight)
+                            constexpr int kElems = RC * kD / kConsumers;
+                            float acc[kElems];
+#pragma unroll
+                            for (int k = 0; k < kElems; ++k) acc[k] = 0.f;
+                            for (int c0 = 0; c0 < nch; c0 += 4) {
+                                int64_t base[4];
+#pragma unroll
+                                for (int cc = 0; cc < 4; ++cc)
+                                    base[cc] = c0 + cc < nch
+                                                   ? (int64_t(chunk_slot(hd.slot0, c0 + cc, full, total_full)) * p.hkv + hd.h) *
+                                                         p.rows * kD
+                                                   : -1;
+#pragma unroll
+                                for (int k = 0; k < kElems; ++k) {
+                                    const int idx = tid + k * kConsumers;
+                                    if (idx < nel) {
+                                        const int r = idx >> 7, d = idx & (kD - 1);
+                                        float x[4];
+#pragma unroll
+                                        for (int cc = 0; cc < 4; ++cc)
+                                            x[cc] = base[cc] >= 0 ? __ldcg(p.part_o + base[cc] + r * kD + d) : 0.f;
+#pragma unroll
+                                        for (int cc = 0; cc < 4; ++cc)
+                                            if (base[cc] >= 0) acc[k] = fmaf(wbuf[(c0 + cc) * p.rows + r], x[cc], acc[k]);
+                                    }
+                                }
+                            }
+#pragma unroll
+                            for (int k = 0; k < kElems; ++k) {
+                                const int idx = tid + k * kConsumers;
+                                if (idx < nel) {
+                                    const int r = idx >> 7, d = idx & (kD - 1);
+                                    const int j = r / p.group, gq = r - j * p.group;
+                                    p.out[((int64_t(hd.b) * p.lq + j) * p.hq + hd.h * p.group + gq) * kD + d] =
+                                        to_bits16<BF16>(acc[k]);
+                                }
+                            }
+                        } else {
+                        // Too many chunks for the weights buffer: one element per thread and round.
                         for (int idx = tid; idx < nel; idx += kConsumers) {
                             const int r = idx >> 7, d = idx & (kD - 1);
                             float L = -INFINITY;
@@ -647,6 +726,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             const int j = r / p.group, gq = r - j * p.group;
                             p.out[((int64_t(hd.b) * p.lq + j) * p.hq + hd.h * p.group + gq) * kD + d] =
                                 to_bits16<BF16>(den > 0.f ? acc / den : 0.f);
+                        }
                         }
                         if (tid == 0) p.counters[hd.b * p.hkv + hd.h] = 0;
                     }
