@@ -974,7 +974,9 @@ def main():
     bufs = [serial_bufs, tuple(torch.empty_like(d) for d in serial_bufs)]
     h_outs = [h_out, torch.empty(out.shape, dtype=out.dtype).pin_memory()]
 
-    def e2e_pipelined(n):
+    def e2e_pipelined(n, keep):
+        """keep collects the steps' outputs: alive until the caller has synchronised, so the
+        allocator never hands a block the copy stream still reads to a later step."""
         ev_up = [torch.cuda.Event(), torch.cuda.Event()]
         ev_done = [torch.cuda.Event(), torch.cuda.Event()]
         cs.wait_stream(stream)
@@ -986,6 +988,7 @@ def main():
             j = i & 1
             stream.wait_event(ev_up[j])
             o = layer(bufs[j])
+            keep.append(o)
             ev_done[j].record(stream)
             with torch.cuda.stream(cs):
                 if i + 1 < n:
@@ -995,7 +998,6 @@ def main():
                         d.copy_(h, non_blocking=True)
                     ev_up[j ^ 1].record(cs)
                 cs.wait_event(ev_done[j])
-                o.record_stream(cs)
                 h_outs[j].copy_(o, non_blocking=True)
         stream.wait_stream(cs)
 
@@ -1014,11 +1016,18 @@ def main():
         barrier()
         return x0.elapsed_time(x1) / n, wall
 
-    e2e_serial(3)
-    e2e_pipelined(3)
     ne = max(10, min(args.steps, 200))
+    e2e_serial(3)
+    # an untimed pass of the same length fills the allocator's pool with the blocks the kept
+    # outputs of the timed pass need (no cudaMalloc inside the timed region)
+    warm = []
+    e2e_pipelined(ne, warm)
+    torch.cuda.synchronize(dev)
+    del warm
     serial_ms, serial_wall_ms = timed_e2e(e2e_serial, ne)
-    e2e_ms, wall_ms = timed_e2e(e2e_pipelined, ne)
+    kept = []
+    e2e_ms, wall_ms = timed_e2e(lambda n: e2e_pipelined(n, kept), ne)
+    del kept
     pctx.reset_context()
 
     # every rank on its own GPU, every rank in the communicator
