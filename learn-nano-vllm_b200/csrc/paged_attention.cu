@@ -263,22 +263,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int64_t max_full = (int64_t(1) << (31 - kRemBits)) - 1;
         if (int64_t(total_tiles) / chunk > max_full) chunk = (int64_t(total_tiles) + max_full - 1) / max_full;
     }
-    int my_full = 0, my_rem = 0;
+    // Both offsets in one scan of the packed count full << kRemBits | rem: the remainder
+    // counts sum to at most the batch (< 2^kRemBits), so no carry reaches the full part.
+    int my_packed = 0;
     for (int b = lo; b < hi; ++b) {
         const SeqChunks sc = seq_chunks(p.context_lens[b], cap, chunk);
-        my_full += sc.full;
-        my_rem += sc.rem;
+        my_packed += (sc.full << kRemBits) + sc.rem;
     }
-    int total_full = 0, total_rem = 0;
-    int ofull = block_exclusive_scan(my_full, sm.red, &total_full);
-    int orem = block_exclusive_scan(my_rem, sm.red, &total_rem);
+    int total_packed = 0;
+    int opacked = block_exclusive_scan(my_packed, sm.red, &total_packed);
     for (int b = lo; b < hi; ++b) {
-        sm.off[b] = (ofull << kRemBits) | orem;
+        sm.off[b] = opacked;
         const SeqChunks sc = seq_chunks(p.context_lens[b], cap, chunk);
-        ofull += sc.full;
-        orem += sc.rem;
+        opacked += (sc.full << kRemBits) + sc.rem;
     }
-    if (tid == 0) sm.off[p.batch] = (total_full << kRemBits) | total_rem;
+    const int total_full = total_packed >> kRemBits, total_rem = total_packed & ((1 << kRemBits) - 1);
+    if (tid == 0) sm.off[p.batch] = total_packed;
     __syncthreads();
     const int total_items = (total_full + total_rem) * p.hkv;
 
