@@ -23,8 +23,9 @@
 // dims; 3 stages, 2 for more than 8 query rows) guarded by full/empty
 // mbarriers, writes a small header per stage describing the tile, and with
 // an item's first tile bulk-copies its query rows into shared memory.  It
-// fetches the next item's metadata (context length, block ids) while the
-// current item streams.  Warps 0-7 are consumers (two per SM sub-partition,
+// claims the next item two tiles before the current one ends and fetches its
+// metadata (context length, block ids) while those tiles stream: one item
+// ahead, never two, so no CTA holds unstarted work while others run dry.  Warps 0-7 are consumers (two per SM sub-partition,
 // so that one hides the other's latency): each takes 16 of the 128 tokens of
 // a stage, computes S = Q K^T and O += P V with mma.sync.m16n8k16 (rows =
 // query rows, padded to 16), and keeps its own online-softmax state (max,
@@ -59,6 +60,7 @@ constexpr size_t kFixedBytes = kCtrlWords * 4 + size_t(kCounterSlots) * 4;
 constexpr int kWaves = 4;
 constexpr int kChunkMaxTiles = 32;           // at most 4096 tokens per item
 constexpr int kRemBits = 12;                 // packed offsets: full-chunk offset << 12 | remainder offset
+constexpr int kClaimAhead = 2;               // tiles before an item's end at which the next one is claimed
 
 struct Header {
     int32_t item, b, h, tile, flags, ctx, nchunks, slot0;
@@ -295,14 +297,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int first_claim = atomicAdd(&p.ctrl[0], 1);
             cur.item = total_items;
             if (first_claim < total_items) fetch_meta(cur, first_claim, p, sm.off, total_full, chunk, cap);
-            int claim = atomicAdd(&p.ctrl[0], 1);
             while (ok && cur.item < total_items) {
                 const int ctx = min(cur.ctx, cap);
                 const int nt = (ctx + kTile - 1) / kTile;
                 const int t0 = cur.t0;
                 const int t1 = int(min(int64_t(nt), t0 + chunk));
                 const int32_t* bt = p.block_tables + int64_t(cur.b) * p.bt_stride;
-                int next_claim = claim;
+                // The next item is claimed kClaimAhead tiles before this one ends: early enough for
+                // its metadata loads to overlap the last tiles, late enough that no CTA sits on an
+                // unstarted item while others run out of work at the end of the launch.
+                const int t_claim = max(t0, t1 - kClaimAhead);
                 nxt.item = total_items;
                 for (int t = t0; t < t1; ++t) {
                     if (!mbar_wait(&sm.empty[stage], phase ^ 1, p.wait_ns)) {
@@ -311,9 +315,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     const bool first = t == t0;
-                    if (first) {  // start fetching the next item while this one streams
+                    if (t == t_claim) {
+                        const int claim = atomicAdd(&p.ctrl[0], 1);
                         if (claim < total_items) fetch_meta(nxt, claim, p, sm.off, total_full, chunk, cap);
-                        next_claim = atomicAdd(&p.ctrl[0], 1);
                     }
                     const int pos = t * kTile;
                     const int lb = pos / p.block_size;
@@ -355,7 +359,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (++stage == NS) { stage = 0; phase ^= 1; }
                 }
                 cur = nxt;
-                claim = next_claim;
             }
             if (ok) {
                 if (mbar_wait(&sm.empty[stage], phase ^ 1, p.wait_ns)) {
