@@ -57,7 +57,7 @@ constexpr int kMaxBatch = 2048;
 constexpr int kCounterSlots = 65536;
 constexpr int kCtrlWords = 64;               // [0] next item, [1] finished CTAs, [2] error word
 constexpr size_t kFixedBytes = kCtrlWords * 4 + size_t(kCounterSlots) * 4;
-constexpr int kWaves = 4;
+constexpr int kWaves = 3;
 constexpr int kChunkMaxTiles = 32;           // at most 4096 tokens per item
 constexpr int kRemBits = 12;                 // packed offsets: full-chunk offset << 12 | remainder offset
 constexpr int kClaimAhead = 2;               // tiles before an item's end at which the next one is claimed
@@ -152,13 +152,17 @@ struct SeqChunks {
     int nt, full, rem;
 };
 
+__device__ __forceinline__ SeqChunks tile_chunks(int nt, int64_t chunk) {
+    SeqChunks s;
+    s.nt = nt;
+    s.full = int(nt / chunk);
+    s.rem = (nt - int64_t(s.full) * chunk) > 0 ? 1 : 0;
+    return s;
+}
+
 __device__ __forceinline__ SeqChunks seq_chunks(int ctx, int cap, int64_t chunk) {
     ctx = min(ctx, cap);
-    SeqChunks s;
-    s.nt = ctx > 0 ? (ctx + kTile - 1) / kTile : 0;
-    s.full = int(s.nt / chunk);
-    s.rem = (s.nt - int64_t(s.full) * chunk) > 0 ? 1 : 0;
-    return s;
+    return tile_chunks(ctx > 0 ? (ctx + kTile - 1) / kTile : 0, chunk);
 }
 
 // Metadata of one claimed work item.  The producer fetches it one item
@@ -232,21 +236,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         prefetch_tmap(&tmv);
     }
 
-    // Rows of CUDA-graph padding (context_lens <= 0) get a zero output.
-    const int64_t row_vec = int64_t(p.lq) * p.hq * kD / 8;  // uint4 per batch row
-    for (int b = blockIdx.x; b < p.batch; b += gridDim.x) {
-        if (p.context_lens[b] <= 0) {
-            uint4* o = reinterpret_cast<uint4*>(p.out) + b * row_vec;
-            for (int64_t i = tid; i < row_vec; i += kThreads) o[i] = make_uint4(0, 0, 0, 0);
-        }
-    }
+    // The producer's first claim does not depend on the plan: its latency overlaps the planning.
+    const bool producer = warp == kConsumerWarps && lane == 0 && !p.idle_producer;
+    const int first_claim = producer ? atomicAdd(&p.ctrl[0], 1) : 0;
 
     // ---- plan: tiles per sequence, chunk length, chunk offsets ----------------
     const int cap = p.bt_stride * p.block_size;  // tokens addressable through the block table
     const int seg = (p.batch + kThreads - 1) / kThreads;
     const int lo = min(tid * seg, p.batch), hi = min(lo + seg, p.batch);
     int my_tiles = 0;
-    for (int b = lo; b < hi; ++b) my_tiles += seq_chunks(p.context_lens[b], cap, 1).nt;
+    for (int b = lo; b < hi; ++b) {
+        const int nt = seq_chunks(p.context_lens[b], cap, 1).nt;
+        sm.off[b] = nt;  // this thread's sequences only; replaced by their offsets below
+        my_tiles += nt;
+    }
     int total_tiles = 0;
     block_exclusive_scan(my_tiles, sm.red, &total_tiles);
     int64_t chunk;
@@ -269,14 +272,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     // counts sum to at most the batch (< 2^kRemBits), so no carry reaches the full part.
     int my_packed = 0;
     for (int b = lo; b < hi; ++b) {
-        const SeqChunks sc = seq_chunks(p.context_lens[b], cap, chunk);
+        const SeqChunks sc = tile_chunks(sm.off[b], chunk);
         my_packed += (sc.full << kRemBits) + sc.rem;
     }
     int total_packed = 0;
     int opacked = block_exclusive_scan(my_packed, sm.red, &total_packed);
     for (int b = lo; b < hi; ++b) {
+        const SeqChunks sc = tile_chunks(sm.off[b], chunk);
         sm.off[b] = opacked;
-        const SeqChunks sc = seq_chunks(p.context_lens[b], cap, chunk);
         opacked += (sc.full << kRemBits) + sc.rem;
     }
     const int total_full = total_packed >> kRemBits, total_rem = total_packed & ((1 << kRemBits) - 1);
@@ -284,9 +287,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     const int total_items = (total_full + total_rem) * p.hkv;
 
+    // Rows without a cached token (context_lens <= 0: CUDA-graph padding) have no items and get
+    // a zero output.
+    const int64_t row_vec = int64_t(p.lq) * p.hq * kD / 8;  // uint4 per batch row
+    for (int b = blockIdx.x; b < p.batch; b += gridDim.x) {
+        if (sm.off[b + 1] == sm.off[b]) {
+            uint4* o = reinterpret_cast<uint4*>(p.out) + b * row_vec;
+            for (int64_t i = tid; i < row_vec; i += kThreads) o[i] = make_uint4(0, 0, 0, 0);
+        }
+    }
+
     if (warp == kConsumerWarps) {
         // ------------------------------------------------------------ producer
-        if (lane == 0 && !p.idle_producer) {
+        if (producer) {
             const uint64_t pol = l2_policy_evict_first();
             const uint32_t q_bytes = uint32_t(p.group) * kD * 2;  // one query token's rows of this kv head
             int stage = 0;
@@ -294,7 +307,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             int64_t fills = 0;
             bool ok = true;
             ItemMeta cur, nxt;
-            const int first_claim = atomicAdd(&p.ctrl[0], 1);
             cur.item = total_items;
             if (first_claim < total_items) fetch_meta(cur, first_claim, p, sm.off, total_full, chunk, cap);
             while (ok && cur.item < total_items) {
@@ -632,104 +644,46 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (sm.flag) {
                         const int nch = hd.nchunks;
                         const int full = nch - (seq_chunks(hd.ctx, cap, chunk).rem);
-                        // The combine buffer is free here: it holds the chunks' weights.
-                        float* wbuf = &sm.co[0][0][0];
-                        constexpr int kWCap = (kConsumerWarps / 2) * RC * kD;
-                        if (nch * p.rows <= kWCap) {
-                            // (1) every chunk's log-sum-exp of every row, all loads in flight at once
-                            for (int i = tid; i < nch * p.rows; i += kConsumers) {
-                                const int c = i / p.rows, r = i - c * p.rows;
-                                const int64_t it = int64_t(chunk_slot(hd.slot0, c, full, total_full)) * p.hkv + hd.h;
-                                wbuf[i] = __ldcg(p.part_lse + it * p.rows + r);
-                            }
-                            if (!consumer_sync(&sm.cbar, cphase, p.wait_ns)) {
-                                atomicOr(&p.ctrl[2], DEV_ERR_WAIT_PEER);
-                                *reinterpret_cast<volatile int32_t*>(&sm.err) = 1;
-                                break;
-                            }
-                            // (2) per row, one warp: weights 2^(lse_c - L) / sum_c, in place
-                            for (int r = warp; r < p.rows; r += kConsumerWarps) {
-                                float L = -INFINITY;
-                                for (int c = lane; c < nch; c += 32) L = fmaxf(L, wbuf[c * p.rows + r]);
-#pragma unroll
-                                for (int o = 16; o >= 1; o >>= 1) L = fmaxf(L, __shfl_xor_sync(0xffffffffu, L, o));
-                                float den = 0.f;
-                                for (int c = lane; c < nch; c += 32) {
-                                    const float w = L == -INFINITY ? 0.f : fast_exp2(wbuf[c * p.rows + r] - L);
-                                    wbuf[c * p.rows + r] = w;
-                                    den += w;
-                                }
-#pragma unroll
-                                for (int o = 16; o >= 1; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
-                                const float inv = den > 0.f ? 1.f / den : 0.f;
-                                for (int c = lane; c < nch; c += 32) wbuf[c * p.rows + r] *= inv;
-                            }
-                            if (!consumer_sync(&sm.cbar, cphase, p.wait_ns)) {
-                                atomicOr(&p.ctrl[2], DEV_ERR_WAIT_PEER);
-                                *reinterpret_cast<volatile int32_t*>(&sm.err) = 1;
-                                break;
-                            }
-                            // (3) outputs: up to kElems elements per thread, the partials of four
-                            // chunks per element loaded together (independent L2 reads in flight)
-                            constexpr int kElems = RC * kD / kConsumers;
-                            float acc[kElems];
-#pragma unroll
-                            for (int k = 0; k < kElems; ++k) acc[k] = 0.f;
+                        // One pass over the chunks, four at a time: every thread merges the
+                        // partials of two output elements at once with a running maximum of the
+                        // chunks' log-sum-exps (base 2), the sixteen loads of a group in flight.
+                        for (int e0 = 2 * tid; e0 < nel; e0 += 2 * kConsumers) {
+                            const int r = e0 >> 7, d = e0 & (kD - 1);  // d even: (d, d + 1) in one row
+                            float mrun = -INFINITY, den = 0.f, acc0 = 0.f, acc1 = 0.f;
                             for (int c0 = 0; c0 < nch; c0 += 4) {
-                                int64_t base[4];
+                                float lse[4];
+                                float2 x[4];
 #pragma unroll
-                                for (int cc = 0; cc < 4; ++cc)
-                                    base[cc] = c0 + cc < nch
-                                                   ? (int64_t(chunk_slot(hd.slot0, c0 + cc, full, total_full)) * p.hkv + hd.h) *
-                                                         p.rows * kD
-                                                   : -1;
-#pragma unroll
-                                for (int k = 0; k < kElems; ++k) {
-                                    const int idx = tid + k * kConsumers;
-                                    if (idx < nel) {
-                                        const int r = idx >> 7, d = idx & (kD - 1);
-                                        float x[4];
-#pragma unroll
-                                        for (int cc = 0; cc < 4; ++cc)
-                                            x[cc] = base[cc] >= 0 ? __ldcg(p.part_o + base[cc] + r * kD + d) : 0.f;
-#pragma unroll
-                                        for (int cc = 0; cc < 4; ++cc)
-                                            if (base[cc] >= 0) acc[k] = fmaf(wbuf[(c0 + cc) * p.rows + r], x[cc], acc[k]);
+                                for (int cc = 0; cc < 4; ++cc) {
+                                    if (c0 + cc < nch) {
+                                        const int64_t it =
+                                            int64_t(chunk_slot(hd.slot0, c0 + cc, full, total_full)) * p.hkv + hd.h;
+                                        lse[cc] = __ldcg(p.part_lse + it * p.rows + r);
+                                        x[cc] = __ldcg(reinterpret_cast<const float2*>(p.part_o + (it * p.rows + r) * kD + d));
+                                    } else {
+                                        lse[cc] = -INFINITY;
+                                        x[cc] = make_float2(0.f, 0.f);
                                     }
                                 }
-                            }
+                                const float mx = fmaxf(fmaxf(mrun, fmaxf(lse[0], lse[1])), fmaxf(lse[2], lse[3]));
+                                if (mx == -INFINITY) continue;
+                                const float sc = mrun == -INFINITY ? 0.f : fast_exp2(mrun - mx);
+                                den *= sc;
+                                acc0 *= sc;
+                                acc1 *= sc;
 #pragma unroll
-                            for (int k = 0; k < kElems; ++k) {
-                                const int idx = tid + k * kConsumers;
-                                if (idx < nel) {
-                                    const int r = idx >> 7, d = idx & (kD - 1);
-                                    const int j = r / p.group, gq = r - j * p.group;
-                                    p.out[((int64_t(hd.b) * p.lq + j) * p.hq + hd.h * p.group + gq) * kD + d] =
-                                        to_bits16<BF16>(acc[k]);
-                                }
-                            }
-                        } else {
-                        // Too many chunks for the weights buffer: one element per thread and round.
-                        for (int idx = tid; idx < nel; idx += kConsumers) {
-                            const int r = idx >> 7, d = idx & (kD - 1);
-                            float L = -INFINITY;
-                            for (int c = 0; c < hd.nchunks; ++c) {
-                                const int64_t it = int64_t(chunk_slot(hd.slot0, c, full, total_full)) * p.hkv + hd.h;
-                                L = fmaxf(L, __ldcg(p.part_lse + it * p.rows + r));
-                            }
-                            float den = 0.f, acc = 0.f;
-                            if (L != -INFINITY) {
-                                for (int c = 0; c < hd.nchunks; ++c) {
-                                    const int64_t it = int64_t(chunk_slot(hd.slot0, c, full, total_full)) * p.hkv + hd.h;
-                                    const float w = fast_exp2(__ldcg(p.part_lse + it * p.rows + r) - L);
+                                for (int cc = 0; cc < 4; ++cc) {
+                                    const float w = lse[cc] == -INFINITY ? 0.f : fast_exp2(lse[cc] - mx);
                                     den += w;
-                                    acc = fmaf(w, __ldcg(p.part_o + (it * p.rows + r) * kD + d), acc);
+                                    acc0 = fmaf(w, x[cc].x, acc0);
+                                    acc1 = fmaf(w, x[cc].y, acc1);
                                 }
+                                mrun = mx;
                             }
+                            const float inv = den > 0.f ? 1.f / den : 0.f;
                             const int j = r / p.group, gq = r - j * p.group;
-                            p.out[((int64_t(hd.b) * p.lq + j) * p.hq + hd.h * p.group + gq) * kD + d] =
-                                to_bits16<BF16>(den > 0.f ? acc / den : 0.f);
-                        }
+                            *reinterpret_cast<uint32_t*>(p.out + ((int64_t(hd.b) * p.lq + j) * p.hq + hd.h * p.group + gq) * kD +
+                                                         d) = pack2<BF16>(acc0 * inv, acc1 * inv);
                         }
                         if (tid == 0) p.counters[hd.b * p.hkv + hd.h] = 0;
                     }
