@@ -180,6 +180,14 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t& r0, uint32_t& r1, uint32_t& 
                  : "r"(addr));
 }
 
+// Transpose of an 8x8 b16 matrix held one 32-bit pair per lane (lane 4r + c holds
+// row r, columns 2c and 2c + 1): the result has the same layout.
+__device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
+    uint32_t y;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
+}
+
 // D(16x8, f32) += A(16x16) * B(16x8), A row-major, B column-major.
 template <bool BF16>
 __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {

@@ -61,6 +61,7 @@ constexpr int kWaves = 3;
 constexpr int kChunkMaxTiles = 32;           // at most 4096 tokens per item
 constexpr int kRemBits = 12;                 // packed offsets: full-chunk offset << 12 | remainder offset
 constexpr int kClaimAhead = 2;               // tiles before an item's end at which the next one is claimed
+constexpr float kLazyMax = 8.f;              // log2 headroom before a row's running maximum is raised
 
 struct Header {
     int32_t item, b, h, tile, flags, ctx, nchunks, slot0;
@@ -397,16 +398,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ------------------------------------------------------------ consumers
         const int g = lane >> 2, t4 = lane & 3;
         const int mi = lane >> 3, rr = lane & 7;
-        const int tok_k = warp * 16 + (mi >> 1) * 8 + rr;  // ldmatrix row of K (token in tile)
-        const int tok_v = warp * 16 + (mi & 1) * 8 + rr;   // ldmatrix row of V
-        const int kadd = mi & 1, vadd = mi >> 1;
+        // ldmatrix rows (token in the tile) and 16-byte column offsets of this lane.  Up to 8 query
+        // rows: tokens are the MMA's M dimension (S^T = K Q^T, O^T += V^T P^T) and the rows its N;
+        // more rows: rows are M (S = Q K^T, O += P V).
+        const int tok_k = ROWS_HI ? warp * 16 + (mi >> 1) * 8 + rr : warp * 16 + (mi & 1) * 8 + rr;
+        const int kadd = ROWS_HI ? (mi & 1) : (mi >> 1);
+        const int tok_v = ROWS_HI ? warp * 16 + (mi & 1) * 8 + rr : warp * 16 + (mi >> 1) * 8 + rr;
+        const int vadd = ROWS_HI ? (mi >> 1) : (mi & 1);
         const float sl2 = p.scale_log2;
         int stage = 0;
         uint32_t phase = 0, cphase = 0;
-        float m_run[2], l_run[2];
-        float o[16][4];
-        uint32_t qa[8][4];
+        // Running maximum (raw score) and sum of the two rows this lane holds: rows g and g + 8
+        // (ROWS_HI) or rows 2 t4 and 2 t4 + 1.  msl = m_run * log2(e) * scale (0 while m_run is -inf).
+        float m_run[2], l_run[2], msl[2];
+        float o[ROWS_HI ? 16 : 8][4];  // O (rows x dims) or O^T (dims x rows) fragments
+        uint32_t qa[8][ROWS_HI ? 4 : 2];  // Q as the A operand, or Q^T as the B operand
         int lim[2];
+        int lim_min = 0;
         while (true) {
             // Exit decisions are warp-uniform (the lanes' waits can disagree at the limit).
             if (!__all_sync(0xffffffffu, mbar_wait(&sm.full[stage], phase, p.wait_ns))) {
@@ -421,21 +429,42 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (hd.item < 0) break;
             if (hd.flags & kFirst) {
                 const uint32_t* qs = reinterpret_cast<const uint32_t*>(sm.qbuf[stage]);
+                if constexpr (ROWS_HI) {
 #pragma unroll
-                for (int hr = 0; hr < 2; ++hr) {
-                    const int r = g + 8 * hr;
-                    const bool valid = (hr == 0 || ROWS_HI) && r < p.rows;
-                    lim[hr] = valid ? hd.ctx - p.lq + r / p.group : -1;
+                    for (int hr = 0; hr < 2; ++hr) {
+                        const int r = g + 8 * hr;
+                        const bool valid = r < p.rows;
+                        lim[hr] = valid ? hd.ctx - p.lq + r / p.group : -1;
+#pragma unroll
+                        for (int kk = 0; kk < 8; ++kk) {
+                            qa[kk][hr] = valid ? qs[r * (kD / 2) + kk * 8 + t4] : 0u;
+                            qa[kk][2 + hr] = valid ? qs[r * (kD / 2) + kk * 8 + 4 + t4] : 0u;
+                        }
+                    }
+                } else {
+                    // B fragment of Q^T: this lane's column is query row g.
+                    const bool valid = g < p.rows;
 #pragma unroll
                     for (int kk = 0; kk < 8; ++kk) {
-                        qa[kk][hr] = valid ? qs[r * (kD / 2) + kk * 8 + t4] : 0u;
-                        qa[kk][2 + hr] = valid ? qs[r * (kD / 2) + kk * 8 + 4 + t4] : 0u;
+                        qa[kk][0] = valid ? qs[g * (kD / 2) + kk * 8 + t4] : 0u;
+                        qa[kk][1] = valid ? qs[g * (kD / 2) + kk * 8 + 4 + t4] : 0u;
                     }
-                    m_run[hr] = -INFINITY;
-                    l_run[hr] = 0.f;
+                    // Padding rows (past p.rows) see the whole context: only rows that exist mask.
+#pragma unroll
+                    for (int j = 0; j < 2; ++j) {
+                        const int r = 2 * t4 + j;
+                        lim[j] = r < p.rows ? hd.ctx - p.lq + r / p.group : hd.ctx - 1;
+                    }
+                    lim_min = hd.ctx - p.lq;  // row 0's limit, the smallest
                 }
 #pragma unroll
-                for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+                for (int hr = 0; hr < 2; ++hr) {
+                    m_run[hr] = -INFINITY;
+                    l_run[hr] = 0.f;
+                    msl[hr] = 0.f;
+                }
+#pragma unroll
+                for (int n = 0; n < (ROWS_HI ? 16 : 8); ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
             }
             const int tok_base = hd.tile * kTile + warp * 16;
             const uint32_t st = smem_u32(sm.stages[stage]);
@@ -454,85 +483,160 @@ __global__ void __launch_bounds__(kThreads, 1)
                     zeroed = true;
                     __syncwarp();
                 }
-                // S = Q K^T for this warp's 16 tokens; two accumulator sets halve the dependent chain
-                float s[2][4], s2[2][4];
+                if constexpr (ROWS_HI) {
+                    // S = Q K^T for this warp's 16 tokens; two accumulator sets halve the dependent chain
+                    float s[2][4], s2[2][4];
 #pragma unroll
-                for (int n = 0; n < 2; ++n)
+                    for (int n = 0; n < 2; ++n)
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) s[n][e] = s2[n][e] = 0.f;
+                        for (int e = 0; e < 4; ++e) s[n][e] = s2[n][e] = 0.f;
 #pragma unroll
-                for (int kk = 0; kk < 8; ++kk) {
-                    const int c16 = 2 * kk + kadd;
-                    const uint32_t addr = st + (kk >> 2) * kHalfBytes + tok_k * 128 + (((c16 & 7) ^ rr) << 4);
-                    uint32_t b0, b1, b2, b3;
-                    ldsm_x4(b0, b1, b2, b3, addr);
-                    if (kk < 4) {
-                        mma_16816<BF16>(s[0], qa[kk], b0, b1);
-                        mma_16816<BF16>(s[1], qa[kk], b2, b3);
-                    } else {
-                        mma_16816<BF16>(s2[0], qa[kk], b0, b1);
-                        mma_16816<BF16>(s2[1], qa[kk], b2, b3);
-                    }
-                }
-#pragma unroll
-                for (int n = 0; n < 2; ++n)
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) s[n][e] += s2[n][e];
-                float pr[2][4];
-                float alpha[2] = {1.f, 1.f};
-#pragma unroll
-                for (int hr = 0; hr < (ROWS_HI ? 2 : 1); ++hr) {
-                    float v[4] = {s[0][2 * hr], s[0][2 * hr + 1], s[1][2 * hr], s[1][2 * hr + 1]};
-                    const int tk[4] = {tok_base + 2 * t4, tok_base + 2 * t4 + 1, tok_base + 8 + 2 * t4,
-                                       tok_base + 9 + 2 * t4};
-#pragma unroll
-                    for (int e = 0; e < 4; ++e)
-                        if (tk[e] > lim[hr]) v[e] = -INFINITY;
-                    float mx = fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3]));
-                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-                    const float mnew = fmaxf(m_run[hr], mx);
-                    const float msl = mnew == -INFINITY ? 0.f : mnew * sl2;
-                    alpha[hr] = mnew == m_run[hr] ? 1.f : fast_exp2(fmaf(m_run[hr], sl2, -msl));
-                    float sum = 0.f;
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        pr[hr][e] = fast_exp2(fmaf(v[e], sl2, -msl));
-                        sum += pr[hr][e];
-                    }
-                    l_run[hr] = fmaf(l_run[hr], alpha[hr], sum);
-                    m_run[hr] = mnew;
-                }
-                // Rescale O only when some row's running max moved (rare after the first tiles).
-                if (__any_sync(0xffffffffu, alpha[0] != 1.f || alpha[1] != 1.f)) {
-#pragma unroll
-                    for (int n = 0; n < 16; ++n) {
-                        o[n][0] *= alpha[0];
-                        o[n][1] *= alpha[0];
-                        if constexpr (ROWS_HI) {
-                            o[n][2] *= alpha[1];
-                            o[n][3] *= alpha[1];
+                    for (int kk = 0; kk < 8; ++kk) {
+                        const int c16 = 2 * kk + kadd;
+                        const uint32_t addr = st + (kk >> 2) * kHalfBytes + tok_k * 128 + (((c16 & 7) ^ rr) << 4);
+                        uint32_t b0, b1, b2, b3;
+                        ldsm_x4(b0, b1, b2, b3, addr);
+                        if (kk < 4) {
+                            mma_16816<BF16>(s[0], qa[kk], b0, b1);
+                            mma_16816<BF16>(s[1], qa[kk], b2, b3);
+                        } else {
+                            mma_16816<BF16>(s2[0], qa[kk], b0, b1);
+                            mma_16816<BF16>(s2[1], qa[kk], b2, b3);
                         }
                     }
-                }
-                uint32_t pa[4];
-                pa[0] = pack2<BF16>(pr[0][0], pr[0][1]);
-                pa[2] = pack2<BF16>(pr[0][2], pr[0][3]);
-                if constexpr (ROWS_HI) {
-                    pa[1] = pack2<BF16>(pr[1][0], pr[1][1]);
-                    pa[3] = pack2<BF16>(pr[1][2], pr[1][3]);
-                } else {
-                    pa[1] = pa[3] = 0u;
-                }
 #pragma unroll
-                for (int pp = 0; pp < 8; ++pp) {
-                    const int c16 = 2 * pp + vadd;
-                    const uint32_t addr =
-                        st + 2 * kHalfBytes + (pp >> 2) * kHalfBytes + tok_v * 128 + (((c16 & 7) ^ rr) << 4);
-                    uint32_t v0, v1, v2, v3;
-                    ldsm_x4_t(v0, v1, v2, v3, addr);
-                    mma_16816<BF16>(o[2 * pp], pa, v0, v1);
-                    mma_16816<BF16>(o[2 * pp + 1], pa, v2, v3);
+                    for (int n = 0; n < 2; ++n)
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) s[n][e] += s2[n][e];
+                    float pr[2][4];
+                    float alpha[2] = {1.f, 1.f};
+#pragma unroll
+                    for (int hr = 0; hr < (ROWS_HI ? 2 : 1); ++hr) {
+                        float v[4] = {s[0][2 * hr], s[0][2 * hr + 1], s[1][2 * hr], s[1][2 * hr + 1]};
+                        const int tk[4] = {tok_base + 2 * t4, tok_base + 2 * t4 + 1, tok_base + 8 + 2 * t4,
+                                           tok_base + 9 + 2 * t4};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e)
+                            if (tk[e] > lim[hr]) v[e] = -INFINITY;
+                        float mx = fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3]));
+                        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+                        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+                        const float mnew = fmaxf(m_run[hr], mx);
+                        const float msl = mnew == -INFINITY ? 0.f : mnew * sl2;
+                        alpha[hr] = mnew == m_run[hr] ? 1.f : fast_exp2(fmaf(m_run[hr], sl2, -msl));
+                        float sum = 0.f;
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            pr[hr][e] = fast_exp2(fmaf(v[e], sl2, -msl));
+                            sum += pr[hr][e];
+                        }
+                        l_run[hr] = fmaf(l_run[hr], alpha[hr], sum);
+                        m_run[hr] = mnew;
+                    }
+                    // Rescale O only when some row's running max moved (rare after the first tiles).
+                    if (__any_sync(0xffffffffu, alpha[0] != 1.f || alpha[1] != 1.f)) {
+#pragma unroll
+                        for (int n = 0; n < 16; ++n) {
+                            o[n][0] *= alpha[0];
+                            o[n][1] *= alpha[0];
+                            if constexpr (ROWS_HI) {
+                                o[n][2] *= alpha[1];
+                                o[n][3] *= alpha[1];
+                            }
+                        }
+                    }
+                    uint32_t pa[4];
+                    pa[0] = pack2<BF16>(pr[0][0], pr[0][1]);
+                    pa[2] = pack2<BF16>(pr[0][2], pr[0][3]);
+                    if constexpr (ROWS_HI) {
+                        pa[1] = pack2<BF16>(pr[1][0], pr[1][1]);
+                        pa[3] = pack2<BF16>(pr[1][2], pr[1][3]);
+                    } else {
+                        pa[1] = pa[3] = 0u;
+                    }
+#pragma unroll
+                    for (int pp = 0; pp < 8; ++pp) {
+                        const int c16 = 2 * pp + vadd;
+                        const uint32_t addr =
+                            st + 2 * kHalfBytes + (pp >> 2) * kHalfBytes + tok_v * 128 + (((c16 & 7) ^ rr) << 4);
+                        uint32_t v0, v1, v2, v3;
+                        ldsm_x4_t(v0, v1, v2, v3, addr);
+                        mma_16816<BF16>(o[2 * pp], pa, v0, v1);
+                        mma_16816<BF16>(o[2 * pp + 1], pa, v2, v3);
+                    }
+                } else {
+                    // S^T = K Q^T: this warp's 16 tokens (M) x 8 query rows (N); two accumulator sets
+                    // halve the dependent chain.  c0/c1: token g, rows 2 t4 / 2 t4 + 1; c2/c3: token g + 8.
+                    float s[4] = {0.f, 0.f, 0.f, 0.f}, s2[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk) {
+                        const int c16 = 2 * kk + kadd;
+                        const uint32_t addr = st + (kk >> 2) * kHalfBytes + tok_k * 128 + (((c16 & 7) ^ rr) << 4);
+                        uint32_t a[4];
+                        ldsm_x4(a[0], a[1], a[2], a[3], addr);
+                        if (kk < 4)
+                            mma_16816<BF16>(s, a, qa[kk][0], qa[kk][1]);
+                        else
+                            mma_16816<BF16>(s2, a, qa[kk][0], qa[kk][1]);
+                    }
+                    float v[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) v[e] = s[e] + s2[e];
+                    if (tok_base + 15 > lim_min) {  // the tile reaches past some row's last visible token
+                        const int ta = tok_base + g, tb = ta + 8;
+                        if (ta > lim[0]) v[0] = -INFINITY;
+                        if (ta > lim[1]) v[1] = -INFINITY;
+                        if (tb > lim[0]) v[2] = -INFINITY;
+                        if (tb > lim[1]) v[3] = -INFINITY;
+                    }
+                    // Exponents relative to the rows' running maxima.  Those are updated (exact tile
+                    // maxima over the warp, O^T and sums rescaled) only when a score exceeds its row's
+                    // maximum by more than 2^kLazyMax, or the row has none yet; otherwise P <= 2^kLazyMax.
+                    float x[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) x[e] = fmaf(v[e], sl2, -msl[e & 1]);
+                    const bool grow = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3])) > kLazyMax ||
+                                      (m_run[0] == -INFINITY && fmaxf(v[0], v[2]) != -INFINITY) ||
+                                      (m_run[1] == -INFINITY && fmaxf(v[1], v[3]) != -INFINITY);
+                    if (__any_sync(0xffffffffu, grow)) {
+                        float tm[2] = {fmaxf(v[0], v[2]), fmaxf(v[1], v[3])};
+#pragma unroll
+                        for (int j = 0; j < 2; ++j) {
+#pragma unroll
+                            for (int sh = 4; sh <= 16; sh <<= 1) tm[j] = fmaxf(tm[j], __shfl_xor_sync(0xffffffffu, tm[j], sh));
+                            const float mnew = fmaxf(m_run[j], tm[j]);
+                            const float mslnew = mnew == -INFINITY ? 0.f : mnew * sl2;
+                            const float alpha = m_run[j] == -INFINITY ? 0.f : fast_exp2(msl[j] - mslnew);
+                            l_run[j] *= alpha;
+#pragma unroll
+                            for (int pp = 0; pp < 8; ++pp) {
+                                o[pp][j] *= alpha;
+                                o[pp][2 + j] *= alpha;
+                            }
+                            m_run[j] = mnew;
+                            msl[j] = mslnew;
+                        }
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) x[e] = fmaf(v[e], sl2, -msl[e & 1]);
+                    }
+                    float pr[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) pr[e] = fast_exp2(x[e]);
+                    l_run[0] += pr[0] + pr[2];
+                    l_run[1] += pr[1] + pr[3];
+                    // P^T as the B operand (16 tokens x 8 rows): transpose the two 8 x 8 blocks.
+                    const uint32_t pb0 = movmatrix_t(pack2<BF16>(pr[0], pr[1]));
+                    const uint32_t pb1 = movmatrix_t(pack2<BF16>(pr[2], pr[3]));
+                    // O^T += V^T P^T, 16 dims per MMA.
+#pragma unroll
+                    for (int pp = 0; pp < 8; ++pp) {
+                        const int c16 = 2 * pp + vadd;
+                        const uint32_t addr =
+                            st + 2 * kHalfBytes + (pp >> 2) * kHalfBytes + tok_v * 128 + (((c16 & 7) ^ rr) << 4);
+                        uint32_t a[4];
+                        ldsm_x4_t(a[0], a[1], a[2], a[3], addr);
+                        mma_16816<BF16>(o[pp], a, pb0, pb1);
+                    }
                 }
             }
             if (zeroed) fence_proxy_async_smem();
@@ -542,16 +646,39 @@ __global__ void __launch_bounds__(kThreads, 1)
 
             if (hd.flags & kLast) {
                 // ---- combine the eight warps' states of this item ----
+                // Row sums over the lanes that hold the same rows (t4 for ROWS_HI, g otherwise).
 #pragma unroll
                 for (int hr = 0; hr < 2; ++hr) {
-                    l_run[hr] += __shfl_xor_sync(0xffffffffu, l_run[hr], 1);
-                    l_run[hr] += __shfl_xor_sync(0xffffffffu, l_run[hr], 2);
+                    if constexpr (ROWS_HI) {
+                        l_run[hr] += __shfl_xor_sync(0xffffffffu, l_run[hr], 1);
+                        l_run[hr] += __shfl_xor_sync(0xffffffffu, l_run[hr], 2);
+                    } else {
+#pragma unroll
+                        for (int sh = 4; sh <= 16; sh <<= 1) l_run[hr] += __shfl_xor_sync(0xffffffffu, l_run[hr], sh);
+                    }
                 }
                 constexpr int kHalf = kConsumerWarps / 2;
                 // 8 -> 4: warps 4-7 hand their state to warps 0-3, which merge it in registers.
-                if (warp >= kHalf) {
+                if constexpr (!ROWS_HI) {
+                  if (warp >= kHalf) {
 #pragma unroll
-                    for (int hr = 0; hr < (ROWS_HI ? 2 : 1); ++hr) {
+                    for (int j = 0; j < 2; ++j) {
+                        const int r = 2 * t4 + j;
+                        if (g == 0) {
+                            sm.cm[warp][r] = m_run[j];
+                            sm.cl[warp][r] = l_run[j];
+                        }
+#pragma unroll
+                        for (int pp = 0; pp < 8; ++pp) {
+                            sm.co[warp - kHalf][r][16 * pp + g] = o[pp][j];
+                            sm.co[warp - kHalf][r][16 * pp + g + 8] = o[pp][2 + j];
+                        }
+                    }
+                  }
+                } else {
+                  if (warp >= kHalf) {
+#pragma unroll
+                    for (int hr = 0; hr < 2; ++hr) {
                         const int r = g + 8 * hr;
                         if (t4 == 0) {
                             sm.cm[warp][r] = m_run[hr];
@@ -562,15 +689,40 @@ __global__ void __launch_bounds__(kThreads, 1)
                             *reinterpret_cast<float2*>(&sm.co[warp - kHalf][r][8 * n + 2 * t4]) =
                                 make_float2(o[n][2 * hr], o[n][2 * hr + 1]);
                     }
+                  }
                 }
                 if (!consumer_sync(&sm.cbar, cphase, p.wait_ns)) {
                     atomicOr(&p.ctrl[2], DEV_ERR_WAIT_PEER);
                     *reinterpret_cast<volatile int32_t*>(&sm.err) = 1;
                     break;
                 }
-                if (warp < kHalf) {
+                if constexpr (!ROWS_HI) {
+                  if (warp < kHalf) {
 #pragma unroll
-                    for (int hr = 0; hr < (ROWS_HI ? 2 : 1); ++hr) {
+                    for (int j = 0; j < 2; ++j) {
+                        const int r = 2 * t4 + j;
+                        const float mb = sm.cm[warp + kHalf][r], lb = sm.cl[warp + kHalf][r];
+                        const float M = fmaxf(m_run[j], mb);
+                        const float sa = M == -INFINITY ? 0.f : fast_exp2((m_run[j] - M) * sl2);
+                        const float sb = M == -INFINITY ? 0.f : fast_exp2((mb - M) * sl2);
+#pragma unroll
+                        for (int pp = 0; pp < 8; ++pp) {
+#pragma unroll
+                            for (int eh = 0; eh < 2; ++eh) {
+                                float* cp = &sm.co[warp][r][16 * pp + g + 8 * eh];
+                                *cp = o[pp][j + 2 * eh] * sa + *cp * sb;
+                            }
+                        }
+                        if (g == 0) {
+                            sm.cm[warp][r] = M;
+                            sm.cl[warp][r] = l_run[j] * sa + lb * sb;
+                        }
+                    }
+                  }
+                } else {
+                  if (warp < kHalf) {
+#pragma unroll
+                    for (int hr = 0; hr < 2; ++hr) {
                         const int r = g + 8 * hr;
                         const float mb = sm.cm[warp + kHalf][r], lb = sm.cl[warp + kHalf][r];
                         const float M = fmaxf(m_run[hr], mb);
@@ -587,6 +739,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             sm.cl[warp][r] = l_run[hr] * sa + lb * sb;
                         }
                     }
+                  }
                 }
                 if (!consumer_sync(&sm.cbar, cphase, p.wait_ns)) {
                     atomicOr(&p.ctrl[2], DEV_ERR_WAIT_PEER);
