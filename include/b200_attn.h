@@ -217,7 +217,8 @@ B200_API int32_t b200_oproj_allreduce_error(void* stream, int32_t* flag);
  * zero-filled once before the first call; every call leaves its control
  * region zeroed again.  Calls sharing a workspace must not overlap on the GPU.
  * Constraints: D == 128, dtype bf16 or fp16, block_size % 128 == 0,
- * batch <= 2048, query_len * (Hq / Hkv) <= 16.
+ * batch <= 2048, query_len * (Hq / Hkv) <= 16, softmax_scale positive and
+ * finite (B200_ERR_ARG otherwise).
  */
 B200_API size_t b200_paged_attention_workspace_size(int32_t max_items, int32_t query_len,
                                            int32_t group_size, int32_t head_dim);

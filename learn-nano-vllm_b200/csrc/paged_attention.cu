@@ -38,6 +38,7 @@
 // which is an mbarrier with one arrival per consumer thread rather than a
 // bar.sync, so that a warp whose sibling left the loop on an error gives up
 // after the limit instead of waiting for it forever.
+#include <cfloat>
 #include <climits>
 #include <mutex>
 
@@ -916,6 +917,8 @@ extern "C" int32_t b200_paged_attention(void* out, const void* q, int64_t q_stri
     B200_REQUIRE(num_heads > 0 && num_kv_heads > 0 && num_heads % num_kv_heads == 0,
                  "paged_attention: num_heads %d not a multiple of num_kv_heads %d", num_heads, num_kv_heads);
     B200_REQUIRE(query_len >= 1, "paged_attention: query_len %d < 1", query_len);
+    B200_REQUIRE(softmax_scale > 0.f && softmax_scale <= FLT_MAX, "paged_attention: softmax_scale %g not positive and finite",
+                 double(softmax_scale));
     const int group = num_heads / num_kv_heads;
     const int rows = query_len * group;
     if (head_dim != kD) return fail(B200_ERR_UNSUPPORTED, "paged_attention: head_dim %d (only 128)", head_dim);
@@ -1118,6 +1121,8 @@ extern "C" int32_t b200_paged_attention_noalloc(void* out, const void* q, int64_
     B200_REQUIRE(num_heads > 0 && num_kv_heads > 0 && num_heads % num_kv_heads == 0,
                  "paged_attention_noalloc: num_heads %d not a multiple of num_kv_heads %d", num_heads, num_kv_heads);
     B200_REQUIRE(query_len >= 1, "paged_attention_noalloc: query_len %d < 1", query_len);
+    B200_REQUIRE(softmax_scale > 0.f && softmax_scale <= FLT_MAX,
+                 "paged_attention_noalloc: softmax_scale %g not positive and finite", double(softmax_scale));
     const int group = num_heads / num_kv_heads;
     const int rows = query_len * group;
     if (head_dim != kD) return fail(B200_ERR_UNSUPPORTED, "paged_attention_noalloc: head_dim %d (only 128)", head_dim);

@@ -49,6 +49,13 @@ def test_argument_errors_mirror_reference_asserts(pkg):
     rc = lib.b200_paged_attention(dummy, dummy, 2048, dummy, dummy, 4, 256, dummy, 4, dummy, 2, 1, 16, 8, 128,
                                   0.1, 1, None, 0, None)
     assert rc == 3
+    for bad_scale in (0.0, -0.1, float("inf"), float("nan")):
+        rc = lib.b200_paged_attention(dummy, dummy, 2048, dummy, dummy, 4, 256, dummy, 4, dummy, 2, 1, 16, 8, 128,
+                                      bad_scale, 1, dummy, 1 << 20, None)
+        assert rc == 1 and b"softmax_scale" in lib.b200_last_error()
+        rc = lib.b200_paged_attention_noalloc(dummy, dummy, 2048, dummy, dummy, 4, 256, dummy, 4, dummy, 2, 1, 16, 8,
+                                              128, bad_scale, 1, None)
+        assert rc == 1 and b"softmax_scale" in lib.b200_last_error()
 
 
 def test_workspace_size():
