@@ -58,7 +58,7 @@ FALLBACK_BF16_TFLOPS = 1590.0
 # -k regex:paged_attention -s 2 -c 1 python bench.py --batch 64 --steps 3 --warmup 1
 # --no-cpu-baseline --no-extras); the full launch is too large to capture with every metric,
 # and its traffic grows in proportion (K/V rows are read once), so traffic is reported scaled.
-DRAM_TRAFFIC_RATIO = 1.033
+DRAM_TRAFFIC_RATIO = 1.032
 
 
 def parse():

@@ -10,9 +10,10 @@
 // call is CUDA-graph capturable): every CTA scans context_lens into shared
 // memory and picks the chunk length (about kWaves items per CTA, at most
 // kChunkMaxTiles tiles, and coarse enough that the items fit the workspace).
-// Items are numbered full-length chunks first, then each sequence's shorter
-// last chunk, and are claimed dynamically from an atomic counter, so that
-// the large items start early and the tail is made of small ones.  Items of a
+// Items are numbered full-length chunks (and remainders of at least half a
+// chunk) first, then the shorter remainders, and are claimed dynamically from
+// an atomic counter, so that the large items start early and the tail is made
+// of small ones.  Items of a
 // sequence that was split write normalised partial outputs plus their
 // log-sum-exp to the workspace; the CTA that finishes the last chunk of a
 // (b, h) merges them (threadfence-reduction pattern) and writes the output.
@@ -61,7 +62,7 @@ constexpr size_t kFixedBytes = kCtrlWords * 4 + size_t(kCounterSlots) * 4;
 constexpr int kWaves = 3;
 constexpr int kChunkMaxTiles = 32;           // at most 4096 tokens per item
 constexpr int kRemBits = 12;                 // packed offsets: full-chunk offset << 12 | remainder offset
-constexpr int kClaimAhead = 2;               // tiles before an item's end at which the next one is claimed
+constexpr int kClaimAhead = 1;               // tiles before an item's end at which the next one is claimed
 constexpr float kLazyMax = 8.f;              // log2 headroom before a row's running maximum is raised
 
 struct Header {
@@ -148,17 +149,25 @@ __device__ __forceinline__ bool consumer_sync(uint64_t* bar, uint32_t& phase, ui
     return __all_sync(0xffffffffu, ok);
 }
 
-// Chunk layout of one sequence: nt tiles cut into `full` chunks of `chunk`
-// tiles and, if nt is not a multiple, one shorter remainder chunk.
+// Chunk layout of one sequence: `full` items in the first region (chunks of
+// `chunk` tiles, the last of them possibly a remainder of at least half a
+// chunk) and `rem` (0 or 1) short remainder in the second.
 struct SeqChunks {
     int nt, full, rem;
 };
 
+// A sequence of nt tiles is cut into chunks of `chunk` tiles and a shorter remainder.  Items
+// are numbered in two regions: first every sequence's full chunks together with its remainder
+// when that is at least half a chunk ("full" count), then the short remainders ("rem"), so that
+// the smallest items come last and the end of a launch is made of them.
 __device__ __forceinline__ SeqChunks tile_chunks(int nt, int64_t chunk) {
     SeqChunks s;
     s.nt = nt;
     s.full = int(nt / chunk);
-    s.rem = (nt - int64_t(s.full) * chunk) > 0 ? 1 : 0;
+    const int64_t rt = nt - int64_t(s.full) * chunk;
+    const bool big = rt > 0 && 2 * rt >= chunk;
+    s.full += big ? 1 : 0;
+    s.rem = (rt > 0 && !big) ? 1 : 0;
     return s;
 }
 
@@ -177,7 +186,7 @@ struct ItemMeta {
 };
 
 // Partial-output slot (chunk index, before the x Hkv + h) of chunk c of
-// sequence b: full chunks are numbered first, remainder chunks after them.
+// sequence b: first-region chunks are numbered first, short remainders after them.
 __device__ __forceinline__ int chunk_slot(int packed_off, int c, int full, int total_full) {
     return c < full ? (packed_off >> kRemBits) + c : total_full + (packed_off & ((1 << kRemBits) - 1));
 }
@@ -266,8 +275,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else {
             chunk = int64_t(1) << 30;
         }
-        // Full-chunk offsets are packed into 31 - kRemBits bits.
-        const int64_t max_full = (int64_t(1) << (31 - kRemBits)) - 1;
+        // First-region offsets are packed into 31 - kRemBits bits (full chunks, plus at most one
+        // remainder per sequence).
+        const int64_t max_full = (int64_t(1) << (31 - kRemBits)) - 1 - kMaxBatch;
         if (int64_t(total_tiles) / chunk > max_full) chunk = (int64_t(total_tiles) + max_full - 1) / max_full;
     }
     // Both offsets in one scan of the packed count full << kRemBits | rem: the remainder
@@ -329,10 +339,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     const bool first = t == t0;
-                    if (t == t_claim) {
-                        const int claim = atomicAdd(&p.ctrl[0], 1);
-                        if (claim < total_items) fetch_meta(nxt, claim, p, sm.off, total_full, chunk, cap);
-                    }
                     const int pos = t * kTile;
                     const int lb = pos / p.block_size;
                     int blk;
@@ -371,6 +377,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     ++fills;
                     if (++stage == NS) { stage = 0; phase ^= 1; }
+                    // After this tile's loads are issued, so that the claim's dependent loads
+                    // overlap them instead of delaying them.
+                    if (t == t_claim) {
+                        const int claim = atomicAdd(&p.ctrl[0], 1);
+                        if (claim < total_items) fetch_meta(nxt, claim, p, sm.off, total_full, chunk, cap);
+                    }
                 }
                 cur = nxt;
             }
