@@ -83,10 +83,11 @@ def parse():
                          "(per-rank kernel efficiency at TP N without N GPUs)")
     ap.add_argument("--batch", type=int, default=BATCH,
                     help="sequences in the batch (profiling runs use a smaller batch; the bench line uses 512)")
-    ap.add_argument("--row-parallel", choices=["nccl", "fused", "none"], default="nccl",
+    ap.add_argument("--row-parallel", choices=["nccl", "b200", "fused", "none"], default="nccl",
                     help="decode at N > 1: the row-parallel step inside the timed region -- nccl: dist.all_reduce "
-                         "of the o_proj output [B, 4096] bf16; fused: o_proj GEMM + all-reduce in one kernel of "
-                         "this package (OprojAllReduce); none: attention only")
+                         "of the o_proj output [B, 4096] bf16; b200: the same all-reduce by this package's "
+                         "two-shot kernel over peer memory (AllReduce); fused: o_proj GEMM + all-reduce in one "
+                         "kernel of this package (OprojAllReduce); none: attention only")
     ap.add_argument("--no-extras", action="store_true",
                     help="decode: leave out the prefill (config 3) and verify (config 4) keys")
     return ap.parse_args()
@@ -876,14 +877,23 @@ def main():
     rp = args.row_parallel if world > 1 else "none"
     hidden = HQ_TOTAL * HEAD_DIM
     y = torch.randn(BATCH, hidden, generator=g, device=dev).to(torch.bfloat16) if rp != "none" else None
-    oproj, wo = None, None
+    oproj, wo, allreduce = None, None, None
+    if rp == "b200":
+        allreduce = pkg.AllReduce(dist.group.WORLD, BATCH * hidden)
     if rp == "fused":
         oproj = pkg.OprojAllReduce(dist.group.WORLD, max_tokens=BATCH, hidden=hidden)
         wo = (torch.randn(hidden, hq * HEAD_DIM, generator=g, device=dev) * 0.02).to(torch.bfloat16)
 
+    if rp == "b200":
+        # o_proj's output built in the symmetric input slot; the next layer reads the result slot
+        y_in, y_out = allreduce.input_buffer(y.numel()), allreduce.result_buffer(y.numel())
+        y_in.copy_(y.view(-1))
+
     def row_parallel():
         if rp == "nccl":
             dist.all_reduce(y)
+        elif rp == "b200":
+            allreduce(y_in, out=y_out)
         elif rp == "fused":
             oproj(out.view(BATCH, hq * HEAD_DIM), wo, out=y)
 
@@ -934,6 +944,8 @@ def main():
     assert pkg.workspace_error(ws) == 0, "device wait timed out"
     if oproj is not None:
         assert oproj.error() == 0, "o_proj all-reduce wait timed out"
+    if allreduce is not None:
+        assert allreduce.error() == 0, "all-reduce wait timed out"
 
     # -- e2e: the user-facing Attention.forward with host inputs and output read-back
     from learn_nano_vllm_b200 import context as pctx
@@ -954,6 +966,8 @@ def main():
         o = attn(b[0], b[1], b[2])
         if rp == "nccl":
             dist.all_reduce(y)
+        elif rp == "b200":
+            allreduce(y_in, out=y_out)
         elif rp == "fused":
             oproj(o.view(BATCH, hq * HEAD_DIM), wo, out=y)
         return o
@@ -1046,10 +1060,10 @@ def main():
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, kern_ms, e2e_ms, rp_ms, wall_ms, serial_ms, serial_wall_ms = t.tolist()
-    if oproj is not None:
+    if oproj is not None or allreduce is not None:
         torch.cuda.synchronize(dev)
         barrier()
-        del oproj
+        del oproj, allreduce
     total_bytes = (dec_b + store_b) * world
     value = total_bytes * args.steps / (ms / 1e3) / 1e9
     peak, peak_kind = measured_peak()
@@ -1064,6 +1078,11 @@ def main():
                 "config": dict(config_dict(world, ctx), **({"rank_shape": f"one GPU running rank 0's shard of tp{shard}"}
                                                         if shard != world else {}),
                                **({"row_parallel": {"nccl": "NCCL all-reduce of the o_proj output [B, 4096] bf16",
+                                                    "b200": "all-reduce of the o_proj output [B, 4096] bf16 by "
+                                                            "this package's two-shot kernel (AllReduce, peer "
+                                                            "loads and stores, no multicast; the output built in "
+                                                            "its symmetric input slot, the result read from its "
+                                                            "result slot)",
                                                     "fused": "o_proj GEMM + all-reduce in one kernel "
                                                              "(OprojAllReduce, peer stores, no multicast)"}[rp]}
                                   if rp != "none" else {})),

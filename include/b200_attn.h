@@ -8,7 +8,7 @@
  * makes each call capturable in a CUDA graph, which is how nano-vLLM runs
  * decode (nanovllm/engine/model_runner.py:222-257).  The diagnostic readers
  * (b200_workspace_error, b200_paged_attention_noalloc_error,
- * b200_varlen_prefill_error, b200_oproj_allreduce_error) synchronise the
+ * b200_varlen_prefill_error, b200_oproj_allreduce_error, b200_allreduce_error) synchronise the
  * stream they are given.
  *
  * Every wait inside a kernel is bounded (1 s).  One that runs out sets a bit
@@ -196,6 +196,32 @@ B200_API int32_t b200_oproj_allreduce(void* out, int64_t ldo, const void* a, int
 B200_API int64_t b200_oproj_allreduce_workspace_size(void);
 
 B200_API int32_t b200_oproj_allreduce_error(void* stream, int32_t* flag);
+
+/*
+ * All-reduce (sum) of a bf16 vector over the ranks of a tensor-parallel group
+ * through memory every rank maps (plain loads and stores over NVLink, no
+ * multicast).  Replaces the NCCL call that ends a row-parallel layer
+ * (nanovllm/layers/linear.py:155, dist.all_reduce(y)) for decode-sized
+ * tensors.  Two shots: each rank reduces one slice of the vector over every
+ * rank's copy (fp32, rank order, one rounding to bf16) and stores it into
+ * every rank's result slot, so all ranks get the same bits.
+ * in / out: n bf16 values of this rank, 16-byte aligned (out may be in);
+ * n % 8 == 0.  bufs[r]: device array of every rank's slot buffer of buf_elems
+ * bf16 values (a multiple of 16, >= 2 n): the input slot is its first half,
+ * the result slot its second; in == this rank's input slot skips the copy in,
+ * out == its result slot the copy out.  flags[r]: every rank's b200_allreduce_flag_words()
+ * uint32 words, zeroed once before the first call.  world <= 8.  The call's
+ * epoch lives in the flag words, so the launch may be captured in a CUDA graph;
+ * every rank makes the same calls in the same order.  Bounded waits set the
+ * error word read by b200_allreduce_error (results of that call undefined).
+ */
+B200_API int32_t b200_allreduce_bf16(void* out, const void* in, int64_t n, void* const* bufs,
+                            int64_t buf_elems, uint32_t* const* flags, int32_t rank,
+                            int32_t world, void* stream);
+
+B200_API int64_t b200_allreduce_flag_words(void);
+
+B200_API int32_t b200_allreduce_error(void* stream, int32_t* flag);
 
 /*
  * Paged multi-query attention over the KV cache: decode (query_len == 1)

@@ -14,6 +14,7 @@ Public API
   sample                    fused temperature + exponential-race sampler
   DecodeMetadata            decode-step metadata built on the device
   OprojAllReduce            tensor-parallel o_proj GEMM fused with its all-reduce over peer memory
+  AllReduce                 two-shot bf16 all-reduce over peer memory (the row-parallel all-reduce)
   install                   patch nano-vLLM to use this package's Attention (options: the fused
                             q/k epilogue, sampler, device decode metadata, row-parallel
                             GEMM + all-reduce, tensor-parallel worker processes)
@@ -24,10 +25,11 @@ from ._native import B200Error, lib
 from .attention import Attention
 from .decode_meta import DecodeMetadata
 from .oproj import OprojAllReduce
+from .allreduce import AllReduce
 from .integrate import install
 from .ops import (flash_attn_varlen_func, flash_attn_with_kvcache, paged_attention, paged_workspace,
                   qk_norm_rope_store, sample, spec_accept, store_kvcache, workspace_error)
 
-__all__ = ["Attention", "B200Error", "DecodeMetadata", "OprojAllReduce", "context", "flash_attn_varlen_func",
+__all__ = ["AllReduce", "Attention", "B200Error", "DecodeMetadata", "OprojAllReduce", "context", "flash_attn_varlen_func",
            "flash_attn_with_kvcache", "install", "lib", "paged_attention", "paged_workspace", "qk_norm_rope_store",
            "sample", "spec_accept", "store_kvcache", "workspace_error"]

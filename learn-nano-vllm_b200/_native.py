@@ -36,6 +36,9 @@ SIGNATURES = {
                                     _P, _I64, _I32, _I32, _P]),
     "b200_oproj_allreduce_workspace_size": (_I64, []),
     "b200_oproj_allreduce_error": (_I32, [_P, ctypes.POINTER(ctypes.c_int32)]),
+    "b200_allreduce_bf16": (_I32, [_P, _P, _I64, _P, _I64, _P, _I32, _I32, _P]),
+    "b200_allreduce_flag_words": (_I64, []),
+    "b200_allreduce_error": (_I32, [_P, ctypes.POINTER(ctypes.c_int32)]),
     "b200_decode_metadata": (_I32, [_P, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _P]),
     "b200_sample_workspace_size": (_SZ, [_I32]),
     "b200_sample": (_I32, [_P, _P, _I64, _I32, _P, _I32, _I32, _P, _I64, ctypes.c_uint64, ctypes.c_uint64, _P, _SZ,

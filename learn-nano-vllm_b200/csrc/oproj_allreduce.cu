@@ -46,6 +46,7 @@
 // zeroed once): [max_units][world] ready epochs, a finished-CTA counter, the
 // last epoch.
 #include "common.cuh"
+#include "peer_sync.cuh"
 #include "tcgen05.cuh"
 
 namespace b200 {
@@ -81,22 +82,6 @@ struct Smem {
 
 __device__ int32_t g_oar_error;
 
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-    uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
-    uint32_t v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
-    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
 // Bulk copy shared -> global (no multicast): start, then wait until the writes are performed.
 // Every thread that wrote the source executed fence_proxy_async_smem() before the barrier
 // that precedes this call.
@@ -108,12 +93,6 @@ __device__ __forceinline__ void bulk_store_wait(void* dst, const void* src, uint
     asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
     asm volatile("fence.proxy.async.global;" ::: "memory");
 }
-
-__device__ __forceinline__ uint32_t next_epoch(uint32_t e) { return e + 1u == 0u ? 2u : e + 1u; }
-// A ready flag shows epoch e: it holds e, or already the next epoch (its writer ran ahead by one
-// call).  Split arrival flags (this GPU, this grid) can only hold e or older.
-template <bool SYS>
-__device__ __forceinline__ bool shows(uint32_t v, uint32_t e) { return v == e || (SYS && v == next_epoch(e)); }
 
 __device__ __forceinline__ uint4 ld_volatile_v4(const uint32_t* p) {
     uint4 v;
@@ -127,27 +106,6 @@ __device__ __forceinline__ void st_volatile_v4(uint32_t* p, uint4 v) {
     asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
                  "r"(v.w)
                  : "memory");
-}
-
-// Whole warp: lane l < n waits until flags[l * stride] shows epoch, all lanes in
-// parallel; true in every lane once all do, false in every lane on timeout.
-template <bool SYS>
-__device__ __forceinline__ bool warp_wait_flags(const uint32_t* flags, int stride, int n, uint32_t epoch) {
-    const int lane = threadIdx.x & 31;
-    auto ok = [&]() {
-        if (lane >= n) return true;
-        const uint32_t* f = flags + lane * stride;
-        return shows<SYS>(SYS ? ld_acquire_sys(f) : ld_acquire_gpu(f), epoch);
-    };
-    bool done = ok();
-    if (__all_sync(0xffffffffu, done)) return true;
-    const uint64_t t0 = global_timer_ns();
-    while (true) {
-        if (!done) done = ok();
-        if (__all_sync(0xffffffffu, done)) return true;
-        if (__shfl_sync(0xffffffffu, global_timer_ns() - t0 > kWaitLimitNs, 0)) return false;
-        __nanosleep(32);
-    }
 }
 
 // Named barrier that returns, to every participating thread, the OR of `pred`:

@@ -18,10 +18,10 @@ def _port():
         return s.getsockname()[1]
 
 
-def run_ranks(world):
+def run_ranks(world, worker=WORKER):
     port = _port()
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
-    procs = [subprocess.Popen([sys.executable, WORKER, str(r), str(world), str(port)], env=env,
+    procs = [subprocess.Popen([sys.executable, worker, str(r), str(world), str(port)], env=env,
                               stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True) for r in range(world)]
     outs = []
     for p in procs:
