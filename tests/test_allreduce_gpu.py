@@ -20,3 +20,8 @@ def test_single_rank(pkg):
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 def test_two_ranks(pkg):
     _run(2, WORKER)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 3, reason="needs more than two GPUs")
+def test_all_ranks(pkg):
+    _run(torch.cuda.device_count(), WORKER)
