@@ -12,9 +12,10 @@ fixed (strong scaling) and ranks exchange nothing on the data path.
 A step is one decode step of that layer: the KV-cache scatter of the 512
 new tokens followed by paged decode attention over every cached token, and
 with N > 1 GPUs the row-parallel all-reduce of the layer's o_proj output
-([512, 4096] bf16, nanovllm/layers/linear.py:152-156) -- NCCL by default,
-or (--row-parallel fused) the o_proj GEMM and the all-reduce in one kernel
-of this package.  The per-rank cache (4.8 GB / N) is far larger than the
+([512, 4096] bf16, nanovllm/layers/linear.py:152-156) -- by default this
+package's two-shot all-reduce over peer memory (AllReduce), with
+--row-parallel nccl the reference's NCCL call, or (--row-parallel fused) the
+o_proj GEMM and the all-reduce in one kernel of this package.  The per-rank cache (4.8 GB / N) is far larger than the
 126 MB L2, so no flush is needed between steps.  Inputs are synthetic
 (random bf16, seeded).
 
@@ -83,7 +84,7 @@ def parse():
                          "(per-rank kernel efficiency at TP N without N GPUs)")
     ap.add_argument("--batch", type=int, default=BATCH,
                     help="sequences in the batch (profiling runs use a smaller batch; the bench line uses 512)")
-    ap.add_argument("--row-parallel", choices=["nccl", "b200", "fused", "none"], default="nccl",
+    ap.add_argument("--row-parallel", choices=["nccl", "b200", "fused", "none"], default="b200",
                     help="decode at N > 1: the row-parallel step inside the timed region -- nccl: dist.all_reduce "
                          "of the o_proj output [B, 4096] bf16; b200: the same all-reduce by this package's "
                          "two-shot kernel over peer memory (AllReduce); fused: o_proj GEMM + all-reduce in one "
