@@ -73,7 +73,7 @@ def parse():
     ap.add_argument("--workload", choices=["decode", "prefill", "verify", "engine", "qknorm", "sample", "oproj"], default="decode",
                     help="decode = config 5 (the bench line); prefill = config 3; verify = config 4; "
                          "engine = config 2 through nano-vLLM's own engine (1 GPU)")
-    ap.add_argument("--engine-attn", choices=["b200", "b200-fused", "b200-fused-all", "b200-full", "b200-full-rp", "flash_attn"], default="b200",
+    ap.add_argument("--engine-attn", choices=["b200", "b200-fused", "b200-fused-all", "b200-full", "b200-full-rp", "b200-full-ar", "flash_attn"], default="b200",
                     help="engine workload: this package's Attention, or the reference's stock flash-attn path")
     ap.add_argument("--engine-model", choices=["qwen3-0.6b", "qwen3-8b"], default="qwen3-0.6b")
     ap.add_argument("--engine-requests", type=int, default=256)
@@ -765,8 +765,10 @@ def run_engine(args, pkg):
     tp = args.engine_tp
     if args.engine_attn.startswith("b200"):
         a = args.engine_attn
-        pkg.install(fuse_qk_epilogue=a != "b200", fuse_sampler=a in ("b200-fused-all", "b200-full", "b200-full-rp"),
-                    device_metadata=a in ("b200-full", "b200-full-rp"), fuse_row_parallel=a == "b200-full-rp",
+        pkg.install(fuse_qk_epilogue=a != "b200",
+                    fuse_sampler=a in ("b200-fused-all", "b200-full", "b200-full-rp", "b200-full-ar"),
+                    device_metadata=a in ("b200-full", "b200-full-rp", "b200-full-ar"),
+                    fuse_row_parallel=a == "b200-full-rp", row_parallel_allreduce=a == "b200-full-ar",
                     workers=tp > 1, worker_setup=("bench:_engine_worker_setup",))
     elif tp > 1:
         # stock path: the spawned ranks still need the stand-in loader and tokenizer

@@ -94,6 +94,43 @@ def _fused_row_parallel_forward(self, x):
     return _RowParallelState.get(n, x.device)(x, self.weight)
 
 
+class _AllReduceState:
+    """The two-shot all-reduce buffers of this process, one per (row width, device), shared by
+    every RowParallelLinear (they run one after another on one stream)."""
+    ops = {}
+    # Decode-sized outputs only (nano-vLLM captures decode graphs up to 512 sequences); prefill
+    # batches keep NCCL.  The buffers are made by the eager decode forward that precedes each
+    # graph capture (model_runner.py:236-246), never during a capture.
+    max_tokens = 512
+
+    @classmethod
+    def get(cls, n, device):
+        key = (n, device)
+        op = cls.ops.get(key)
+        if op is None:
+            import torch.distributed as dist
+            from .allreduce import AllReduce
+            op = cls.ops[key] = AllReduce(dist.group.WORLD, cls.max_tokens * n, device=device)
+        return op
+
+
+def _allreduce_row_parallel_forward(self, x):
+    """RowParallelLinear.forward (nanovllm/layers/linear.py:152-156) with the reference's F.linear
+    and, for contiguous 16-byte aligned bf16 outputs of at most max_tokens rows, this package's
+    two-shot all-reduce over peer memory (allreduce.AllReduce) in place of dist.all_reduce.  Every
+    rank sees the same batch and layer shapes, so every rank takes the same branch."""
+    import torch.distributed as dist
+    y = torch.nn.functional.linear(x, self.weight, self.bias if self.tp_rank == 0 else None)
+    if self.tp_size > 1:
+        rows = y.numel() // y.shape[-1] if y.dim() else 0
+        if (y.dtype == torch.bfloat16 and y.dim() >= 1 and y.is_contiguous() and 0 < rows <= _AllReduceState.max_tokens
+                and y.numel() % 8 == 0 and y.data_ptr() % 16 == 0):
+            _AllReduceState.get(y.shape[-1], y.device)(y.view(-1))
+        else:
+            dist.all_reduce(y)
+    return y
+
+
 class _FusedSamplerState:
     """Seed and per-call offset of the fused sampler's counter-based noise."""
     seed = 0
@@ -109,7 +146,8 @@ def _fused_sampler_forward(self, logits, temperatures):
 
 
 def install(fuse_qk_epilogue: bool = False, fuse_sampler: bool = False, workers: bool = False,
-            worker_setup: tuple = (), device_metadata: bool = False, fuse_row_parallel: bool = False):
+            worker_setup: tuple = (), device_metadata: bool = False, fuse_row_parallel: bool = False,
+            row_parallel_allreduce: bool = False):
     """Patch the importable `nanovllm` package; returns the patched modules.
 
     With fuse_qk_epilogue, Qwen3Attention.forward also runs q/k RMSNorm, RoPE and
@@ -121,7 +159,10 @@ def install(fuse_qk_epilogue: bool = False, fuse_sampler: bool = False, workers:
     the device from one packed host-to-device copy (decode_meta).  With
     fuse_row_parallel, RowParallelLinear.forward (o_proj, down_proj) runs its GEMM and
     the tensor-parallel all-reduce as one kernel over peer memory (oproj); every rank must run
-    it, so it implies workers.  With workers, the
+    it, so it implies workers.  With row_parallel_allreduce (and not fuse_row_parallel),
+    RowParallelLinear.forward keeps F.linear and replaces its NCCL all-reduce with this
+    package's two-shot all-reduce (allreduce.AllReduce) for decode-sized outputs; it too implies
+    workers.  With workers, the
     engine's tensor-parallel ranks (spawned processes, nanovllm/engine/llm_engine.py:24-30)
     run install() with the same options before building their ModelRunner;
     worker_setup lists "module:function" hooks they run first.
@@ -151,13 +192,16 @@ def install(fuse_qk_epilogue: bool = False, fuse_sampler: bool = False, workers:
     linear_mod = importlib.import_module("nanovllm.layers.linear")
     if not _ORIGINAL_ROW:
         _ORIGINAL_ROW.append(linear_mod.RowParallelLinear.forward)
-    linear_mod.RowParallelLinear.forward = _fused_row_parallel_forward if fuse_row_parallel else _ORIGINAL_ROW[0]
-    if workers or fuse_row_parallel:
+    linear_mod.RowParallelLinear.forward = (_fused_row_parallel_forward if fuse_row_parallel else
+                                            _allreduce_row_parallel_forward if row_parallel_allreduce else
+                                            _ORIGINAL_ROW[0])
+    if workers or fuse_row_parallel or row_parallel_allreduce:
         import functools
         entry = importlib.import_module("__graft_entry__")
         opts = {"setup": list(worker_setup),
                 "install": {"fuse_qk_epilogue": fuse_qk_epilogue, "fuse_sampler": fuse_sampler,
-                            "device_metadata": device_metadata, "fuse_row_parallel": fuse_row_parallel}}
+                            "device_metadata": device_metadata, "fuse_row_parallel": fuse_row_parallel,
+                            "row_parallel_allreduce": row_parallel_allreduce}}
         engine_mod.ModelRunner = functools.partial(entry.nanovllm_worker, options=opts)
     else:
         engine_mod.ModelRunner = runner_mod.ModelRunner

@@ -86,6 +86,38 @@ def _worker(rank, world, port, ret):
         layer.tp_size = world
         ok = all(got == want for _, got, want in results)
         assert stand_in.calls == [((40, 256 // world), (512, 256 // world))], stand_in.calls
+
+        # install(row_parallel_allreduce=True): F.linear kept, the all-reduce of decode-sized bf16
+        # outputs through the two-shot kernel (a stand-in that all-reduces in place here)
+        ar_calls = []
+
+        def ar_stand_in(v):
+            ar_calls.append(tuple(v.shape))
+            dist.all_reduce(v)
+            return v
+
+        integrate._AllReduceState.get = classmethod(lambda cls, n, dev: ar_stand_in)
+        ar_fwd = integrate._allreduce_row_parallel_forward
+
+        def run_ar(x, lay=layer):
+            n0 = len(ar_calls)
+            y = ar_fwd(lay, x)
+            y_ref = stock(lay, x)
+            return len(ar_calls) - n0, torch.equal(y, y_ref)
+
+        ar_results = [("bf16 decode rows", run_ar(x), (1, True)),
+                      ("fp32 output", run_ar(x.float().contiguous(), _fp32_copy(layer, linear)), (0, True)),
+                      ("bias", run_ar(x, with_bias), (1, True))]
+        old = integrate._AllReduceState.max_tokens
+        integrate._AllReduceState.max_tokens = 39
+        ar_results.append(("rows above max_tokens", run_ar(x), (0, True)))
+        integrate._AllReduceState.max_tokens = old
+        layer.tp_size = 1
+        ar_results.append(("tp_size 1", run_ar(x), (0, True)))
+        layer.tp_size = world
+        ok = ok and all(got == want for _, got, want in ar_results)
+        assert ar_calls == [(40 * 512,), (40 * 512,)], ar_calls
+        results += ar_results
         ret[rank] = ok or [r for r in results if r[1] != r[2]]
     except Exception as e:  # reported to the parent
         ret[rank] = repr(e)
