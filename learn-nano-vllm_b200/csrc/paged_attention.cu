@@ -23,16 +23,20 @@
 // with 128-byte swizzle into a ring of 64 KiB stages (K lo/hi dims, V lo/hi
 // dims; 3 stages, 2 for more than 8 query rows) guarded by full/empty
 // mbarriers, writes a small header per stage describing the tile, and with
-// an item's first tile bulk-copies its query rows into shared memory.  It
-// claims the next item two tiles before the current one ends and fetches its
-// metadata (context length, block ids) while those tiles stream: one item
-// ahead, never two, so no CTA holds unstarted work while others run dry.  Warps 0-7 are consumers (two per SM sub-partition,
-// so that one hides the other's latency): each takes 16 of the 128 tokens of
-// a stage, computes S = Q K^T and O += P V with mma.sync.m16n8k16 (rows =
-// query rows, padded to 16), and keeps its own online-softmax state (max,
-// sum, O) in registers with warp-shuffle row reductions; the eight partial
-// states are combined through shared memory at the end of an item (8 -> 4
-// in registers, then 4 -> 1).
+// an item's first tile bulk-copies its query rows into shared memory.  After
+// issuing an item's last tile it claims the next item and fetches its
+// metadata (context length, block ids) while the issued tiles stream: one
+// item ahead, never two, so no CTA holds unstarted work while others run dry.
+// Warps 0-7 are consumers (two per SM sub-partition, so that one hides the
+// other's latency): each takes 16 of the 128 tokens of a stage and computes
+// the scores and P V with mma.sync.m16n8k16.  Up to 8 query rows the tile is
+// transposed -- tokens are the MMA's M and the query rows its N of 8
+// (S^T = K Q^T, O^T += V^T P^T, P^T turned into a B operand by movmatrix) --
+// and a row's running maximum is raised only when a score exceeds it by more
+// than 2^kLazyMax; more rows use rows as M (S = Q K^T, O += P V, padded to
+// 16).  Each warp keeps its own online-softmax state (max, sum, O) in
+// registers; the eight partial states are combined through shared memory at
+// the end of an item (8 -> 4 in registers, then 4 -> 1).
 //
 // Every wait in the kernel is bounded (kWaitLimitNs, or the test limit): the
 // stage barriers, and the consumer warps' own barrier around the combine,
