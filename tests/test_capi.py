@@ -58,6 +58,28 @@ def test_argument_errors_mirror_reference_asserts(pkg):
         assert rc == 1 and b"softmax_scale" in lib.b200_last_error()
 
 
+def test_allreduce_argument_errors(pkg):
+    """b200_allreduce_bf16 rejects bad arguments before it touches memory or launches."""
+    lib = pkg.lib()
+    d = ctypes.c_void_p(256)
+    assert lib.b200_allreduce_bf16(d, d, 0, d, 0, d, 0, 2, None) == 0  # n = 0: no-op
+    rc = lib.b200_allreduce_bf16(None, d, 64, d, 128, d, 0, 2, None)
+    assert rc == 1 and b"null" in lib.b200_last_error()
+    rc = lib.b200_allreduce_bf16(d, d, 64, d, 128, d, 2, 2, None)
+    assert rc == 1 and b"rank" in lib.b200_last_error()
+    rc = lib.b200_allreduce_bf16(d, d, 64, d, 128, d, 0, 9, None)
+    assert rc == 1 and b"rank" in lib.b200_last_error()
+    rc = lib.b200_allreduce_bf16(d, d, 60, d, 128, d, 0, 2, None)
+    assert rc == 1 and b"multiple of 8" in lib.b200_last_error()
+    rc = lib.b200_allreduce_bf16(ctypes.c_void_p(264), d, 64, d, 128, d, 0, 2, None)
+    assert rc == 1 and b"aligned" in lib.b200_last_error()
+    rc = lib.b200_allreduce_bf16(d, d, 64, d, 112, d, 0, 2, None)
+    assert rc == 1 and b"symmetric buffer" in lib.b200_last_error()
+    rc = lib.b200_allreduce_bf16(d, d, 64, d, 136, d, 0, 2, None)
+    assert rc == 1 and b"multiple of 16" in lib.b200_last_error()
+    assert lib.b200_allreduce_flag_words() >= 2 * 8 * 148 + 2
+
+
 def test_workspace_size():
     import __graft_entry__
     lib = __graft_entry__.load_package().lib()
