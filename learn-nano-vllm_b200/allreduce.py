@@ -60,6 +60,12 @@ class AllReduce:
         if out is None:
             out = x
         assert out.dtype == torch.bfloat16 and out.is_contiguous() and out.numel() == x.numel()
+        # inside the slot buffer only as the slots themselves (the kernel copies by CTA ranges)
+        lo, hi = self.bufs.data_ptr(), self.bufs.data_ptr() + self.bufs.numel() * 2
+        for t, ok in ((x, (lo, lo + self.max_elems * 2)), (out, (lo, lo + self.max_elems * 2))):
+            p = t.data_ptr()
+            assert not (lo <= p < hi or lo < p + t.numel() * 2 <= hi) or p in ok, \
+                "tensors inside the slot buffer must start at input_buffer() or result_buffer()"
         rc = lib().b200_allreduce_bf16(out.data_ptr(), x.data_ptr(), x.numel(), self.buf_ptrs.data_ptr(),
                                        self.buf_elems, self.flag_ptrs.data_ptr(), self.rank, self.world,
                                        torch.cuda.current_stream(x.device).cuda_stream)
