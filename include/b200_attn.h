@@ -209,7 +209,8 @@ B200_API int32_t b200_oproj_allreduce_error(void* stream, int32_t* flag);
  * n % 8 == 0.  bufs[r]: device array of every rank's slot buffer of buf_elems
  * bf16 values (a multiple of 16, >= 2 n): the input slot is its first half,
  * the result slot its second; in == this rank's input slot skips the copy in,
- * out == its result slot the copy out.  flags[r]: every rank's b200_allreduce_flag_words()
+ * out == its result slot the copy out.  in and out may each be either slot's
+ * start or memory outside the slot buffer, no other place inside it.  flags[r]: every rank's b200_allreduce_flag_words()
  * uint32 words, zeroed once before the first call.  world <= 8.  The call's
  * epoch lives in the flag words, so the launch may be captured in a CUDA graph;
  * every rank makes the same calls in the same order.  Bounded waits set the
