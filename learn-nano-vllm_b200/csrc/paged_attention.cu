@@ -331,9 +331,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int t0 = cur.t0;
                 const int t1 = int(min(int64_t(nt), t0 + chunk));
                 const int32_t* bt = p.block_tables + int64_t(cur.b) * p.bt_stride;
-                // The next item is claimed kClaimAhead tiles before this one ends: early enough for
-                // its metadata loads to overlap the last tiles, late enough that no CTA sits on an
-                // unstarted item while others run out of work at the end of the launch.
+                // The next item is claimed once the loads of tile t1 - kClaimAhead are issued: its
+                // metadata loads overlap the tiles in flight, and no CTA sits on an unstarted item
+                // while others run out of work at the end of the launch.
                 const int t_claim = max(t0, t1 - kClaimAhead);
                 nxt.item = total_items;
                 for (int t = t0; t < t1; ++t) {
